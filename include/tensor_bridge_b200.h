@@ -1,0 +1,199 @@
+/*
+ * tensor_bridge_b200.h -- C ABI of the B200 (sm_100a) decode + GEMM path.
+ *
+ * The reference (tensor-bridge) exposes its hot path as C++ __global__
+ * kernels that callers forward-declare and launch themselves
+ * (bench/bench.cu:20-23, bench/bench_fused.cu:25-31,
+ * bench/bench_formats.cu:30).  This header replaces those launch sites with
+ * plain C entry points.  Conventions shared by every entry point:
+ *
+ *   - all pointers are DEVICE pointers owned by the caller, except where a
+ *     parameter says "host";
+ *   - every call is asynchronous on the given stream (NULL = legacy default
+ *     stream, which is what the reference uses) and returns a status; a
+ *     non-TB_OK status means nothing was launched;
+ *   - matrices are row-major.  D[M x N] = A[M x K] * B^T with B stored
+ *     [N x K] -- the reference's layout for gemm_fp16_wmma (A row-major,
+ *     B "col-major K x N", src/gemm.cu:44-52).  For the weight-only case A is
+ *     the quantized weight [out_features x in_features] and B the FP16
+ *     activations [tokens x in_features], so N = tokens;
+ *   - any M, N >= 1 is accepted (the reference needs multiples of 16); K
+ *     must be a multiple of 16 (32 for packed FP4);
+ *   - decoded values are bit-identical to the reference's conversion
+ *     primitives (include/tensor_bridge/{fp8,fp4,bf16,tf32}.h), and GEMMs
+ *     accumulate FP32 products of those FP16 values;
+ *   - the library keeps no state besides cached launch attributes and a
+ *     per-device error word (tb_device_error), and is safe to call from
+ *     several host threads on different streams.
+ */
+#ifndef TENSOR_BRIDGE_B200_H
+#define TENSOR_BRIDGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream. */
+typedef struct CUstream_st* tb_stream_t;
+
+typedef enum tb_status {
+    TB_OK = 0,
+    TB_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad enum, negative size */
+    TB_ERR_SHAPE = 2,            /* shape not supported by this entry point */
+    TB_ERR_ALIGNMENT = 3,        /* pointer or row pitch not aligned as required */
+    TB_ERR_CUDA = 4,             /* a CUDA runtime or driver call failed */
+    TB_ERR_LAUNCH = 5,           /* kernel launch failed */
+    TB_ERR_TIMEOUT = 6,          /* a device-side bounded wait expired */
+    TB_ERR_UNSUPPORTED = 7,      /* device is not sm_100, or format not supported here */
+    TB_ERR_WORKSPACE = 8,        /* workspace missing or too small */
+    TB_ERR_NCCL = 9              /* NCCL unavailable or an NCCL call failed */
+} tb_status;
+
+/* Storage formats.  Element counts are in values, not bytes. */
+typedef enum tb_format {
+    TB_FMT_F16 = 0,          /* IEEE binary16, 2 bytes */
+    TB_FMT_E4M3 = 1,         /* FP8 E4M3, 1 byte (include/tensor_bridge/fp8.h) */
+    TB_FMT_E5M2 = 2,         /* FP8 E5M2, 1 byte */
+    TB_FMT_E2M1 = 3,         /* FP4 E2M1 packed two per byte, FIRST value in the HIGH
+                                nibble (reference order, fp4.h:37-43) */
+    TB_FMT_E2M1_UNPACKED = 4,/* FP4 E2M1 one value per byte in the low nibble (the
+                                reference's decode_fp4_to_half input,
+                                bench/bench_formats.cu:51-56) */
+    TB_FMT_BF16 = 5,         /* bfloat16 bits, 2 bytes */
+    TB_FMT_TF32 = 6,         /* TF32 carried in a 32-bit word (tf32.h:22) */
+    TB_FMT_E2M1_HW = 7       /* FP4 E2M1 packed two per byte, FIRST value in the LOW
+                                nibble (tensor-core order); native GEMM only */
+} tb_format;
+
+typedef enum tb_out_type {
+    TB_OUT_F32 = 0,          /* FP32 output (the reference's only output type) */
+    TB_OUT_F16 = 1           /* FP16 output, round-to-nearest-even */
+} tb_out_type;
+
+/* ---- status and device checks ------------------------------------------ */
+
+/* Human-readable name of a status. */
+const char* tb_status_string(tb_status s);
+
+/* Detail of the most recent failure on the calling host thread ("" if none). */
+const char* tb_last_error(void);
+
+/* TB_OK if `device` is an sm_100 GPU this library was built for. */
+tb_status tb_device_supported(int device);
+
+/* Read (and optionally clear) the error word that kernels set when a bounded
+ * device-side wait expires.  Synchronises the device.  *code = 0 means none. */
+tb_status tb_device_error(int* code, int clear);
+
+/* ---- decode streamers ---------------------------------------------------- */
+
+/* dst[i] = decode(src[i]) as FP16 bits, i < n.  Bit-exact to the reference
+ * primitive of `fmt`: fp8_e4m3_to_half (fp8.h:23-31), fp8_e5m2_to_half
+ * (fp8.h:34-39), fp4_e2m1_to_half (fp4.h:33-35; packed order fp4.h:37-43),
+ * bf16_to_half (bf16.h:22-34), tf32_to_half (tf32.h:22-34).  TB_FMT_F16 is a
+ * copy.  Replaces the per-element decode kernels of src/gemm.cu:25-30 and
+ * bench/bench_formats.cu:33-56 (their A half). */
+tb_status tb_decode(tb_format fmt, const void* src, uint16_t* dst, size_t n, tb_stream_t stream);
+
+/* Decode and transpose: src is [rows x cols] row-major in `fmt`, dst is
+ * [cols x rows] row-major FP16.  Replaces the B half of the reference decode
+ * kernels, which write B16[col*K + k] from B[k*N + col] (src/gemm.cu:29).
+ * Packed FP4 needs an even `cols`. */
+tb_status tb_decode_transposed(tb_format fmt, const void* src, uint16_t* dst,
+                               int rows, int cols, tb_stream_t stream);
+
+/* Reference-shaped decode entry points: A [M x K] decoded straight into
+ * A16 [M x K], B [K x N] decoded transposed into B16 [N x K].  Either pair may
+ * be NULL to skip that operand.  Mirror, in order:
+ *   decode_fp8_to_half      src/gemm.cu:25-30 (== decode_fp8_to_half_fmt,
+ *                           bench/bench_formats.cu:45-50)
+ *   decode_bf16_to_half     bench/bench_formats.cu:33-38
+ *   decode_tf32_to_half     bench/bench_formats.cu:39-44
+ *   decode_fp4_to_half      bench/bench_formats.cu:51-56 (one nibble per byte) */
+tb_status tb_decode_fp8_to_half(const uint8_t* A, const uint8_t* B, uint16_t* A16, uint16_t* B16,
+                                int M, int N, int K, tb_stream_t stream);
+tb_status tb_decode_bf16_to_half(const uint16_t* A, const uint16_t* B, uint16_t* A16, uint16_t* B16,
+                                 int M, int N, int K, tb_stream_t stream);
+tb_status tb_decode_tf32_to_half(const uint32_t* A, const uint32_t* B, uint16_t* A16, uint16_t* B16,
+                                 int M, int N, int K, tb_stream_t stream);
+tb_status tb_decode_fp4_to_half(const uint8_t* A, const uint8_t* B, uint16_t* A16, uint16_t* B16,
+                                int M, int N, int K, tb_stream_t stream);
+
+/* ---- GEMMs (tcgen05 tensor cores, TMEM accumulators) --------------------- */
+
+/* D = alpha * A * B^T.  A [M x K] FP16, B [N x K] FP16, FP32 accumulation.
+ * Replaces gemm_fp16_wmma (src/gemm.cu:44-56), which is this call with
+ * out = TB_OUT_F32 and alpha = 1. */
+tb_status tb_gemm_f16(const uint16_t* A, const uint16_t* B, void* D, int M, int N, int K,
+                      tb_out_type out, float alpha, tb_stream_t stream);
+
+/* Weight-only fused GEMM: D = alpha * decode(A) * B^T, A stored in `a_fmt`
+ * (E4M3, E5M2, E2M1, E2M1_UNPACKED, BF16, TF32), B FP16 [N x K].  The kernel
+ * brings raw A tiles into shared memory with TMA and decodes them there to
+ * FP16 operand tiles; decoded weights never reach global memory.  alpha is
+ * the per-tensor dequantisation 1/scale that the reference applies on the
+ * host (bench/bench_formats.cu:164).  The W_q @ X_fp16 case the reference
+ * runs unfused (bench/bench_formats.cu:153-156); its fused kernel
+ * gemm_fp8_fused_fp16 (src/gemm_fused.cu:24-49) quantizes both operands, see
+ * tb_gemm_fp8_fused_fp16 for that one.
+ * `workspace` (device, may be NULL when tb_gemm_fused_workspace returns 0)
+ * holds split-K partial sums for short-and-wide shapes. */
+tb_status tb_gemm_fused(tb_format a_fmt, const void* A, const uint16_t* B, void* D,
+                        int M, int N, int K, tb_out_type out, float alpha,
+                        void* workspace, size_t workspace_bytes, tb_stream_t stream);
+
+/* Bytes of workspace tb_gemm_fused needs for this shape (0 if none). */
+size_t tb_gemm_fused_workspace(tb_format a_fmt, int M, int N, int K);
+
+/* Both operands quantized, run natively by tcgen05 kind::f8f6f4:
+ * D = alpha * A * B^T with A [M x K] in a_fmt and B [N x K] in b_fmt, where
+ * (a_fmt, b_fmt) is (E4M3, E4M3) or (E2M1_HW, E2M1_HW).  alpha is
+ * 1/(scale_A*scale_B).  The tensor core reads E4M3 codes with exponent 0 as
+ * subnormals where the reference decoder flushes them to zero; the
+ * reference quantizer (fp32_to_fp8_e4m3, fp8.h:58) never emits such codes.
+ * Use tb_fp4_repack_hw to turn reference-packed FP4 into TB_FMT_E2M1_HW. */
+tb_status tb_gemm_native(tb_format a_fmt, const void* A, tb_format b_fmt, const void* B, void* D,
+                         int M, int N, int K, tb_out_type out, float alpha, tb_stream_t stream);
+
+/* Swap the two nibbles of every byte: reference FP4 packing (first value high)
+ * <-> tensor-core packing (first value low).  n_bytes bytes, may be in place. */
+tb_status tb_fp4_repack_hw(const uint8_t* src, uint8_t* dst, size_t n_bytes, tb_stream_t stream);
+
+/* Mirror of gemm_fp8_fused_fp16 (src/gemm_fused.cu:24-49): A [M x K] E4M3,
+ * B [K x N] E4M3 (row-major, as the reference reads it), D [M x N] FP32.
+ * Both operands are decoded with the reference rules.  B is decoded and
+ * transposed into `workspace` (N*K*2 bytes, see tb_gemm_fp8_fused_workspace),
+ * A is decoded inside the GEMM. */
+tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, int M, int N, int K,
+                                 void* workspace, size_t workspace_bytes, tb_stream_t stream);
+size_t tb_gemm_fp8_fused_workspace(int M, int N, int K);
+
+/* ---- column-sharded weight GEMM over NCCL -------------------------------- */
+/* The reference is single-GPU; this is the B200 addition for weights too large
+ * or slow for one GPU.  The weight's M rows (output features) are split into
+ * world*chunks row blocks of Mc = M/(world*chunks) rows; rank r owns blocks
+ * c*world + r for c = 0..chunks-1 (block-cyclic), stored back to back in
+ * A_shard [chunks*Mc x K].  For each c the rank computes its block of D with
+ * the fused kernel straight into D at global row (c*world + r)*Mc, then an
+ * in-place NCCL all-gather of block group c (rows [c*world*Mc, (c+1)*world*Mc))
+ * runs on `comm_stream` while block c+1 is computed on `stream`.  On return
+ * (after both streams drain) every rank holds the full D [M x N].  `comm` is
+ * an ncclComm_t from tb_nccl_comm_init; rank and world come from it.  M must
+ * be a multiple of world*chunks*128. */
+tb_status tb_gemm_sharded_fused(tb_format a_fmt, const void* A_shard, const uint16_t* B, void* D,
+                                int M, int N, int K, tb_out_type out, float alpha, void* comm,
+                                int chunks, tb_stream_t stream, tb_stream_t comm_stream);
+
+/* NCCL plumbing (NCCL is loaded at run time; TB_ERR_NCCL if absent). */
+tb_status tb_nccl_unique_id(uint8_t id_out[128]);
+tb_status tb_nccl_comm_init(void** comm_out, int world, int rank, const uint8_t id[128]);
+tb_status tb_nccl_comm_destroy(void* comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TENSOR_BRIDGE_B200_H */

@@ -1,0 +1,149 @@
+"""CPU oracle for the decode + GEMM path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+module, and only to check or time the CUDA path; the product never calls it.
+
+Two libraries, both built by oracle/Makefile:
+  liboracle.so      plain-C restatement of tensor-bridge's conversion
+                    primitives and decode -> FP16 -> FP32-accumulate GEMM
+                    (tb_oracle.c, each function citing the reference lines);
+  _ref/libtbref.so  tensor-bridge's own headers compiled as host code
+                    (ref_shim.cu); present only where the reference checkout
+                    was available at build time.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libtbref.so")
+
+F16, E4M3, E5M2, E2M1, E2M1_UNPACKED, BF16, TF32, E2M1_HW = range(8)
+FORMAT_MAX = {E4M3: 448.0, E5M2: 57344.0, E2M1: 6.0, E2M1_UNPACKED: 6.0, E2M1_HW: 6.0}
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO):
+            raise RuntimeError(f"{ORACLE_SO} missing; run `make -C oracle`")
+        l = ctypes.CDLL(ORACLE_SO)
+        p, sz, i, f = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_float
+        l.oracle_decode.argtypes = [i, p, p, sz]
+        l.oracle_quantize.argtypes = [i, p, p, sz, f]
+        l.oracle_gemm.argtypes = [i, p, i, p, p, i, i, i, i, i, f, i, i]
+        l.oracle_f32_to_f16.restype = ctypes.c_uint16
+        l.oracle_f32_to_f16.argtypes = [f]
+        _lib = l
+    return _lib
+
+
+def ref_lib():
+    """The reference's own primitives, or None when _ref was not built."""
+    global _ref
+    if _ref is None and os.path.exists(REF_SO):
+        l = ctypes.CDLL(REF_SO)
+        p, sz, i, f = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_float
+        for name in ("ref_e4m3_to_half", "ref_e5m2_to_half", "ref_bf16_to_half", "ref_tf32_to_half",
+                     "ref_fp32_to_e4m3", "ref_fp32_to_e5m2", "ref_fp32_to_e2m1", "ref_half_to_e2m1",
+                     "ref_fp32_to_bf16", "ref_half_to_bf16", "ref_fp32_to_tf32", "ref_fp32_to_half"):
+            getattr(l, name).argtypes = [p, p, sz]
+        l.ref_cpu_decode_gemm.argtypes = [i, p, p, p, i, i, i, i, i, f, i]
+        _ref = l
+    return _ref
+
+
+def _c(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def stored_dtype(fmt: int):
+    return {F16: np.uint16, BF16: np.uint16, TF32: np.uint32}.get(fmt, np.uint8)
+
+
+def stored_count(fmt: int, n: int) -> int:
+    return (n + 1) // 2 if fmt in (E2M1, E2M1_HW) else n
+
+
+def decode(fmt: int, src: np.ndarray, n: int) -> np.ndarray:
+    src = np.ascontiguousarray(src)
+    out = np.empty(n, dtype=np.uint16)
+    lib().oracle_decode(fmt, _c(src), _c(out), n)
+    return out
+
+
+def quantize(fmt: int, x: np.ndarray, scale: float = 1.0) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.size
+    out = np.empty(stored_count(fmt, n), dtype=stored_dtype(fmt))
+    lib().oracle_quantize(fmt, _c(x.ravel()), _c(out), n, float(scale))
+    return out.reshape(x.shape[:-1] + (-1,)) if x.ndim > 1 else out
+
+
+def f32_to_f16_bits(x: np.ndarray) -> np.ndarray:
+    return quantize(F16, x).view(np.uint16)
+
+
+def f16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    """FP16 bits -> FP32; every NaN becomes 0x7FFFFFFF, as CUDA's __half2float."""
+    out = np.asarray(h, dtype=np.uint16).view(np.float16).astype(np.float32)
+    out[np.isnan(out)] = np.uint32(0x7FFFFFFF).view(np.float32)
+    return out
+
+
+def gemm(a_fmt: int, A: np.ndarray, b_fmt: int, B: np.ndarray, M: int, N: int, K: int, rows=None,
+         alpha: float = 1.0, out_f16: bool = False, threads: int = 0) -> np.ndarray:
+    """alpha * decode(A)[rows] @ decode(B).T with FP32 accumulation in k order.
+    B is [N x K] in b_fmt.  Returns float32 (or float16 bits as uint16)."""
+    r0, r1 = (0, M) if rows is None else rows
+    A = np.ascontiguousarray(A)
+    B = np.ascontiguousarray(B)
+    out = np.empty((r1 - r0, N), dtype=np.uint16 if out_f16 else np.float32)
+    lib().oracle_gemm(a_fmt, _c(A), b_fmt, _c(B), _c(out), M, N, K, r0, r1, float(alpha), int(out_f16), threads)
+    return out
+
+
+def ref_cpu_gemm(a_fmt: int, A: np.ndarray, B16: np.ndarray, M: int, N: int, K: int, rows=None,
+                 alpha: float = 1.0, threads: int = 0) -> np.ndarray:
+    """The reference's CPU path (its decode primitives + its FP32 loop)."""
+    r = ref_lib()
+    if r is None:
+        raise RuntimeError("oracle/_ref was not built (needs the reference checkout at build time)")
+    r0, r1 = (0, M) if rows is None else rows
+    out = np.empty((r1 - r0, N), dtype=np.float32)
+    r.ref_cpu_decode_gemm(a_fmt, _c(np.ascontiguousarray(A)), _c(np.ascontiguousarray(B16)), _c(out), M, N, K, r0, r1,
+                          float(alpha), threads)
+    return out
+
+
+def rel_frob(x: np.ndarray, ref: np.ndarray) -> float:
+    """sqrt(sum (x-ref)^2 / sum ref^2) in float64 (bench/bench_formats.cu:97-103)."""
+    x = np.asarray(x, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    den = float(np.sum(ref * ref))
+    return float(np.sqrt(np.sum((x - ref) ** 2) / den)) if den > 0 else float(np.sqrt(np.sum((x - ref) ** 2)))
+
+
+# ---- seeded synthetic inputs (shared by tests, smoke and bench) -----------------------
+
+def uniform(seed: int, shape, lo=-1.0, hi=1.0) -> np.ndarray:
+    return np.random.default_rng(seed).uniform(lo, hi, size=shape).astype(np.float32)
+
+
+def normal(seed: int, shape, std=1.0) -> np.ndarray:
+    return np.random.default_rng(seed).normal(0.0, std, size=shape).astype(np.float32)
+
+
+def per_tensor_scale(x: np.ndarray, fmt: int) -> float:
+    """FORMAT_MAX / maxabs as in bench/bench_formats.cu:128-130 (1.0 for BF16/TF32/F16)."""
+    if fmt not in FORMAT_MAX:
+        return 1.0
+    m = float(np.max(np.abs(x))) if x.size else 0.0
+    return float(np.float32(FORMAT_MAX[fmt]) / np.float32(m if m > 0 else 1.0))

@@ -1,0 +1,196 @@
+"""tensor_bridge_b200 -- Python binding of the C ABI in include/tensor_bridge_b200.h.
+
+The product is the shared library libtensor_bridge_b200.so (CUDA kernels for
+sm_100a behind extern "C" entry points).  This module loads it with ctypes,
+declares every entry point's signature, raises TBError on a non-OK status,
+and offers small helpers that take anything with a ``data_ptr()`` (torch
+tensors) or plain integer device addresses.
+
+There is no fallback: if the library is missing, importing works but the
+first call raises LibraryNotBuilt.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtensor_bridge_b200.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "tensor_bridge_b200.h")
+
+
+class Format(enum.IntEnum):
+    F16 = 0
+    E4M3 = 1
+    E5M2 = 2
+    E2M1 = 3            # packed, first value in the high nibble (reference order)
+    E2M1_UNPACKED = 4   # one value per byte
+    BF16 = 5
+    TF32 = 6
+    E2M1_HW = 7         # packed, first value in the low nibble (tensor-core order)
+
+
+class Out(enum.IntEnum):
+    F32 = 0
+    F16 = 1
+
+
+class Status(enum.IntEnum):
+    OK = 0
+    INVALID_ARGUMENT = 1
+    SHAPE = 2
+    ALIGNMENT = 3
+    CUDA = 4
+    LAUNCH = 5
+    TIMEOUT = 6
+    UNSUPPORTED = 7
+    WORKSPACE = 8
+    NCCL = 9
+
+
+class LibraryNotBuilt(RuntimeError):
+    pass
+
+
+class TBError(RuntimeError):
+    def __init__(self, status: int, func: str, detail: str):
+        self.status = Status(status) if status in Status._value2member_map_ else status
+        super().__init__(f"{func}: {getattr(self.status, 'name', status)}: {detail}")
+
+
+# Bytes per stored element, as (numerator, denominator).
+STORED_BYTES = {
+    Format.F16: (2, 1), Format.E4M3: (1, 1), Format.E5M2: (1, 1), Format.E2M1: (1, 2),
+    Format.E2M1_UNPACKED: (1, 1), Format.BF16: (2, 1), Format.TF32: (4, 1), Format.E2M1_HW: (1, 2),
+}
+
+
+def stored_bytes(fmt: Format, n: int) -> int:
+    num, den = STORED_BYTES[Format(fmt)]
+    return (n * num + den - 1) // den
+
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_sz = ctypes.c_size_t
+_f = ctypes.c_float
+_st = ctypes.c_int  # tb_status
+
+# name -> (restype, argtypes); the set of names is exactly the header's.
+SIGNATURES = {
+    "tb_status_string": (ctypes.c_char_p, [_st]),
+    "tb_last_error": (ctypes.c_char_p, []),
+    "tb_device_supported": (_st, [_i]),
+    "tb_device_error": (_st, [ctypes.POINTER(_i), _i]),
+    "tb_decode": (_st, [_i, _p, _p, _sz, _p]),
+    "tb_decode_transposed": (_st, [_i, _p, _p, _i, _i, _p]),
+    "tb_decode_fp8_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
+    "tb_decode_bf16_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
+    "tb_decode_tf32_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
+    "tb_decode_fp4_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
+    "tb_gemm_f16": (_st, [_p, _p, _p, _i, _i, _i, _i, _f, _p]),
+    "tb_gemm_fused": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
+    "tb_gemm_fused_workspace": (_sz, [_i, _i, _i, _i]),
+    "tb_gemm_native": (_st, [_i, _p, _i, _p, _p, _i, _i, _i, _i, _f, _p]),
+    "tb_fp4_repack_hw": (_st, [_p, _p, _sz, _p]),
+    "tb_gemm_fp8_fused_fp16": (_st, [_p, _p, _p, _i, _i, _i, _p, _sz, _p]),
+    "tb_gemm_fp8_fused_workspace": (_sz, [_i, _i, _i]),
+    "tb_gemm_sharded_fused": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _i, _p, _p]),
+    "tb_nccl_unique_id": (_st, [ctypes.c_char_p]),
+    "tb_nccl_comm_init": (_st, [ctypes.POINTER(_p), _i, _i, ctypes.c_char_p]),
+    "tb_nccl_comm_destroy": (_st, [_p]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libtensor_bridge_b200.so once and declare its signatures."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise LibraryNotBuilt(f"{LIB_PATH} is missing; run `make -C tensor-bridge_b200` (or __graft_entry__.build())")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(l, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = l
+    return _lib
+
+
+def _ptr(x):
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return torch.cuda.current_stream().cuda_stream
+        except ImportError:
+            pass
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _check(status: int, func: str):
+    if status != 0:
+        detail = lib().tb_last_error().decode(errors="replace")
+        raise TBError(status, func, detail)
+
+
+def call(name: str, *args):
+    """Call an entry point by name and raise TBError on a non-OK status."""
+    fn = getattr(lib(), name)
+    st = fn(*args)
+    if SIGNATURES[name][0] is _st:
+        _check(st, name)
+    return st
+
+
+# ---- helpers over device buffers ------------------------------------------------------
+
+def decode(fmt, src, dst, n: int, stream=None):
+    call("tb_decode", int(fmt), _ptr(src), _ptr(dst), n, _stream(stream))
+
+
+def decode_transposed(fmt, src, dst, rows: int, cols: int, stream=None):
+    call("tb_decode_transposed", int(fmt), _ptr(src), _ptr(dst), rows, cols, _stream(stream))
+
+
+def gemm_f16(A, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):
+    call("tb_gemm_f16", _ptr(A), _ptr(B), _ptr(D), M, N, K, int(out), alpha, _stream(stream))
+
+
+def fused_workspace_bytes(fmt, M: int, N: int, K: int) -> int:
+    return lib().tb_gemm_fused_workspace(int(fmt), M, N, K)
+
+
+def gemm_fused(fmt, A, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, workspace=None,
+               workspace_bytes: int = 0, stream=None):
+    call("tb_gemm_fused", int(fmt), _ptr(A), _ptr(B), _ptr(D), M, N, K, int(out), alpha, _ptr(workspace),
+         workspace_bytes, _stream(stream))
+
+
+def gemm_native(a_fmt, A, b_fmt, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):
+    call("tb_gemm_native", int(a_fmt), _ptr(A), int(b_fmt), _ptr(B), _ptr(D), M, N, K, int(out), alpha,
+         _stream(stream))
+
+
+def fp4_repack_hw(src, dst, n_bytes: int, stream=None):
+    call("tb_fp4_repack_hw", _ptr(src), _ptr(dst), n_bytes, _stream(stream))
+
+
+def device_error(clear: bool = True) -> int:
+    code = ctypes.c_int(0)
+    call("tb_device_error", ctypes.byref(code), 1 if clear else 0)
+    return code.value

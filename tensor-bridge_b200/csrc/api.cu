@@ -1,0 +1,265 @@
+// api.cu -- the extern "C" boundary (include/tensor_bridge_b200.h): argument
+// checks, status codes, and dispatch to the decode and GEMM launchers.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <cuda_runtime.h>
+#include "tensor_bridge_b200.h"
+#include "tb_host.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+tb_status fail(tb_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+tb_status fail(tb_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return s;
+}
+
+tb_status from_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return TB_OK;
+    return fail(TB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+tb_status check_device() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(TB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    const tb::DeviceInfo& d = tb::device_info(dev);
+    if (d.major != 10 || d.minor != 0)
+        return fail(TB_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", dev, d.major, d.minor);
+    return TB_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool known_format(int f) { return f >= TB_FMT_F16 && f <= TB_FMT_E2M1_HW; }
+
+// Common GEMM shape checks.  K must be a multiple of 16 (32 for packed FP4)
+// so that every operand row pitch is a multiple of 16 bytes (TMA rule).
+tb_status check_gemm_shape(int M, int N, int K, int a_fmt) {
+    if (M <= 0 || N <= 0 || K <= 0) return fail(TB_ERR_SHAPE, "M, N, K must be positive (got %d, %d, %d)", M, N, K);
+    const int kmul = (a_fmt == TB_FMT_E2M1 || a_fmt == TB_FMT_E2M1_HW) ? 32 : 16;
+    if (K % kmul != 0) return fail(TB_ERR_SHAPE, "K = %d must be a multiple of %d for this format", K, kmul);
+    return TB_OK;
+}
+
+tb_status launch_gemm(const tb::GemmRequest& r, cudaStream_t st) {
+    const char* why = nullptr;
+    cudaError_t e = tb::gemm_launch(r, st, &why);
+    if (e == cudaSuccess) return TB_OK;
+    if (why) return fail(TB_ERR_UNSUPPORTED, "%s", why);
+    return fail(TB_ERR_LAUNCH, "GEMM launch: %s", cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tb_status_string(tb_status s) {
+    switch (s) {
+        case TB_OK: return "TB_OK";
+        case TB_ERR_INVALID_ARGUMENT: return "TB_ERR_INVALID_ARGUMENT";
+        case TB_ERR_SHAPE: return "TB_ERR_SHAPE";
+        case TB_ERR_ALIGNMENT: return "TB_ERR_ALIGNMENT";
+        case TB_ERR_CUDA: return "TB_ERR_CUDA";
+        case TB_ERR_LAUNCH: return "TB_ERR_LAUNCH";
+        case TB_ERR_TIMEOUT: return "TB_ERR_TIMEOUT";
+        case TB_ERR_UNSUPPORTED: return "TB_ERR_UNSUPPORTED";
+        case TB_ERR_WORKSPACE: return "TB_ERR_WORKSPACE";
+        case TB_ERR_NCCL: return "TB_ERR_NCCL";
+    }
+    return "TB_ERR_UNKNOWN";
+}
+
+const char* tb_last_error(void) { return g_last_error.c_str(); }
+
+tb_status tb_device_supported(int device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n)
+        return fail(TB_ERR_UNSUPPORTED, "no CUDA device %d", device);
+    const tb::DeviceInfo& d = tb::device_info(device);
+    if (d.major != 10 || d.minor != 0) return fail(TB_ERR_UNSUPPORTED, "device %d is sm_%d%d", device, d.major, d.minor);
+    return TB_OK;
+}
+
+tb_status tb_device_error(int* code, int clear) {
+    if (!code) return fail(TB_ERR_INVALID_ARGUMENT, "code is NULL");
+    tb_status s = from_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    if (s != TB_OK) return s;
+    int v = 0;
+    s = from_cuda(tb::device_error_read(&v), "read device error word");
+    if (s != TB_OK) return s;
+    *code = v;
+    if (clear && v) {
+        s = from_cuda(tb::device_error_clear(), "clear device error word");
+    }
+    return s;
+}
+
+// ---- decode ------------------------------------------------------------------
+
+tb_status tb_decode(tb_format fmt, const void* src, uint16_t* dst, size_t n, tb_stream_t stream) {
+    if (!known_format(fmt) || fmt == TB_FMT_E2M1_HW) return fail(TB_ERR_INVALID_ARGUMENT, "bad format %d", (int)fmt);
+    if (n == 0) return TB_OK;
+    if (!src || !dst) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    const int sms = tb::device_info(tb::current_device()).sms;
+    return from_cuda(tb::decode_launch(fmt, src, dst, n, stream, sms), "decode launch");
+}
+
+tb_status tb_decode_transposed(tb_format fmt, const void* src, uint16_t* dst, int rows, int cols, tb_stream_t stream) {
+    if (!known_format(fmt) || fmt == TB_FMT_E2M1_HW) return fail(TB_ERR_INVALID_ARGUMENT, "bad format %d", (int)fmt);
+    if (rows < 0 || cols < 0) return fail(TB_ERR_SHAPE, "negative shape");
+    if (rows == 0 || cols == 0) return TB_OK;
+    if (fmt == TB_FMT_E2M1 && (cols & 1)) return fail(TB_ERR_SHAPE, "packed FP4 needs an even column count");
+    if (!src || !dst) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    return from_cuda(tb::decode_transposed_launch(fmt, src, dst, rows, cols, stream), "transposed decode launch");
+}
+
+static tb_status decode_pair(tb_format fmt, const void* A, const void* B, uint16_t* A16, uint16_t* B16, int M, int N,
+                             int K, tb_stream_t stream) {
+    if (M < 0 || N < 0 || K < 0) return fail(TB_ERR_SHAPE, "negative shape");
+    if ((A == nullptr) != (A16 == nullptr) || (B == nullptr) != (B16 == nullptr))
+        return fail(TB_ERR_INVALID_ARGUMENT, "each operand needs both its source and destination");
+    tb_status s = TB_OK;
+    if (A) s = tb_decode(fmt, A, A16, static_cast<size_t>(M) * K, stream);
+    if (s == TB_OK && B) s = tb_decode_transposed(fmt, B, B16, K, N, stream);
+    return s;
+}
+
+tb_status tb_decode_fp8_to_half(const uint8_t* A, const uint8_t* B, uint16_t* A16, uint16_t* B16, int M, int N, int K,
+                                tb_stream_t stream) {
+    return decode_pair(TB_FMT_E4M3, A, B, A16, B16, M, N, K, stream);
+}
+tb_status tb_decode_bf16_to_half(const uint16_t* A, const uint16_t* B, uint16_t* A16, uint16_t* B16, int M, int N,
+                                 int K, tb_stream_t stream) {
+    return decode_pair(TB_FMT_BF16, A, B, A16, B16, M, N, K, stream);
+}
+tb_status tb_decode_tf32_to_half(const uint32_t* A, const uint32_t* B, uint16_t* A16, uint16_t* B16, int M, int N,
+                                 int K, tb_stream_t stream) {
+    return decode_pair(TB_FMT_TF32, A, B, A16, B16, M, N, K, stream);
+}
+tb_status tb_decode_fp4_to_half(const uint8_t* A, const uint8_t* B, uint16_t* A16, uint16_t* B16, int M, int N, int K,
+                                tb_stream_t stream) {
+    return decode_pair(TB_FMT_E2M1_UNPACKED, A, B, A16, B16, M, N, K, stream);
+}
+
+tb_status tb_fp4_repack_hw(const uint8_t* src, uint8_t* dst, size_t n_bytes, tb_stream_t stream) {
+    if (n_bytes == 0) return TB_OK;
+    if (!src || !dst) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    const int sms = tb::device_info(tb::current_device()).sms;
+    return from_cuda(tb::fp4_repack_launch(src, dst, n_bytes, stream, sms), "repack launch");
+}
+
+// ---- GEMMs -------------------------------------------------------------------
+
+tb_status tb_gemm_f16(const uint16_t* A, const uint16_t* B, void* D, int M, int N, int K, tb_out_type out, float alpha,
+                      tb_stream_t stream) {
+    tb_status s = check_gemm_shape(M, N, K, TB_FMT_F16);
+    if (s != TB_OK) return s;
+    if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    if (out != TB_OUT_F32 && out != TB_OUT_F16) return fail(TB_ERR_INVALID_ARGUMENT, "bad output type");
+    if (!aligned16(A) || !aligned16(B)) return fail(TB_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+    s = check_device();
+    if (s != TB_OK) return s;
+    tb::GemmRequest r{};
+    r.kind = tb::GemmKind::kF16;
+    r.a_fmt = TB_FMT_F16;
+    r.A = A; r.B = B; r.D = D; r.ldd = N;
+    r.M = M; r.N = N; r.K = K;
+    r.out_f16 = out == TB_OUT_F16;
+    r.alpha = alpha;
+    return launch_gemm(r, stream);
+}
+
+size_t tb_gemm_fused_workspace(tb_format a_fmt, int M, int N, int K) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    return tb::gemm_workspace_bytes(tb::GemmKind::kFused, a_fmt, M, N, K, tb::device_info(dev).sms);
+}
+
+static tb_status fused_request(tb_format a_fmt, const void* A, const uint16_t* B, void* D, long long ldd, int M, int N,
+                               int K, tb_out_type out, float alpha, void* ws, size_t ws_bytes, tb_stream_t stream) {
+    if (a_fmt != TB_FMT_E4M3 && a_fmt != TB_FMT_E5M2 && a_fmt != TB_FMT_E2M1 && a_fmt != TB_FMT_E2M1_UNPACKED &&
+        a_fmt != TB_FMT_BF16 && a_fmt != TB_FMT_TF32 && a_fmt != TB_FMT_F16)
+        return fail(TB_ERR_INVALID_ARGUMENT, "format %d is not a fused weight format", (int)a_fmt);
+    tb_status s = check_gemm_shape(M, N, K, a_fmt);
+    if (s != TB_OK) return s;
+    if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    if (out != TB_OUT_F32 && out != TB_OUT_F16) return fail(TB_ERR_INVALID_ARGUMENT, "bad output type");
+    if (!aligned16(A) || !aligned16(B)) return fail(TB_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+    s = check_device();
+    if (s != TB_OK) return s;
+    tb::GemmRequest r{};
+    r.kind = a_fmt == TB_FMT_F16 ? tb::GemmKind::kF16 : tb::GemmKind::kFused;
+    r.a_fmt = a_fmt;
+    r.A = A; r.B = B; r.D = D; r.ldd = ldd;
+    r.M = M; r.N = N; r.K = K;
+    r.out_f16 = out == TB_OUT_F16;
+    r.alpha = alpha;
+    r.workspace = ws;
+    r.workspace_bytes = ws_bytes;
+    return launch_gemm(r, stream);
+}
+
+tb_status tb_gemm_fused(tb_format a_fmt, const void* A, const uint16_t* B, void* D, int M, int N, int K,
+                        tb_out_type out, float alpha, void* workspace, size_t workspace_bytes, tb_stream_t stream) {
+    return fused_request(a_fmt, A, B, D, N, M, N, K, out, alpha, workspace, workspace_bytes, stream);
+}
+
+tb_status tb_gemm_native(tb_format a_fmt, const void* A, tb_format b_fmt, const void* B, void* D, int M, int N, int K,
+                         tb_out_type out, float alpha, tb_stream_t stream) {
+    if (!(a_fmt == TB_FMT_E4M3 && b_fmt == TB_FMT_E4M3))
+        return fail(TB_ERR_UNSUPPORTED, "native GEMM supports (E4M3, E4M3) in this build");
+    tb_status s = check_gemm_shape(M, N, K, a_fmt);
+    if (s != TB_OK) return s;
+    if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    if (out != TB_OUT_F32 && out != TB_OUT_F16) return fail(TB_ERR_INVALID_ARGUMENT, "bad output type");
+    if (!aligned16(A) || !aligned16(B)) return fail(TB_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+    s = check_device();
+    if (s != TB_OK) return s;
+    tb::GemmRequest r{};
+    r.kind = tb::GemmKind::kNative;
+    r.a_fmt = a_fmt;
+    r.A = A; r.B = B; r.D = D; r.ldd = N;
+    r.M = M; r.N = N; r.K = K;
+    r.out_f16 = out == TB_OUT_F16;
+    r.alpha = alpha;
+    return launch_gemm(r, stream);
+}
+
+size_t tb_gemm_fp8_fused_workspace(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const size_t bt = (static_cast<size_t>(N) * K * 2 + 255) / 256 * 256;
+    return bt + tb_gemm_fused_workspace(TB_FMT_E4M3, M, N, K);
+}
+
+tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, int M, int N, int K, void* workspace,
+                                 size_t workspace_bytes, tb_stream_t stream) {
+    tb_status s = check_gemm_shape(M, N, K, TB_FMT_E4M3);
+    if (s != TB_OK) return s;
+    if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    const size_t bt = (static_cast<size_t>(N) * K * 2 + 255) / 256 * 256;
+    if (!workspace || workspace_bytes < bt)
+        return fail(TB_ERR_WORKSPACE, "workspace needs at least %zu bytes", bt);
+    uint16_t* B16 = static_cast<uint16_t*>(workspace);
+    s = tb_decode_transposed(TB_FMT_E4M3, B, B16, K, N, stream);
+    if (s != TB_OK) return s;
+    return tb_gemm_fused(TB_FMT_E4M3, A, B16, D, M, N, K, TB_OUT_F32, 1.0f, static_cast<uint8_t*>(workspace) + bt,
+                         workspace_bytes - bt, stream);
+}
+
+}  // extern "C"

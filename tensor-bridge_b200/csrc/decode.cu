@@ -1,0 +1,246 @@
+// decode.cu -- standalone decode kernels (stored format -> FP16 in HBM).
+//
+// These replace the reference's one-element-per-thread decode kernels
+// (src/gemm.cu:25-30, bench/bench_formats.cu:33-56).  The straight kernel is
+// a grid-stride HBM streamer: each thread step loads 16-byte input units with
+// 128-bit loads and writes the decoded FP16 with 128-bit stores, two units in
+// flight per thread.  The transposed kernel (the reference's B operand,
+// B16[col*K + k] = decode(B[k*N + col])) goes through a 32 x 64 shared-memory
+// tile so both the reads and the writes are coalesced.
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "tb_decode.cuh"
+#include "gemm_kernel.cuh"
+#include "tb_host.h"
+
+namespace tb {
+
+// Per-format geometry of one 16-byte input unit.
+template <int FMT> struct Unit;
+template <> struct Unit<kE4M3> { static constexpr int kIn = 1, kOut = 2, kElems = 16; };
+template <> struct Unit<kE5M2> { static constexpr int kIn = 1, kOut = 2, kElems = 16; };
+template <> struct Unit<kE2M1U> { static constexpr int kIn = 1, kOut = 2, kElems = 16; };
+template <> struct Unit<kE2M1> { static constexpr int kIn = 1, kOut = 4, kElems = 32; };
+template <> struct Unit<kBF16> { static constexpr int kIn = 1, kOut = 1, kElems = 8; };
+template <> struct Unit<kTF32> { static constexpr int kIn = 2, kOut = 1, kElems = 8; };
+template <> struct Unit<kF16> { static constexpr int kIn = 1, kOut = 1, kElems = 8; };
+
+template <int FMT>
+__device__ __forceinline__ void decode_vec(const uint4 (&in)[Unit<FMT>::kIn], uint4 (&out)[Unit<FMT>::kOut]) {
+    if constexpr (FMT == kE4M3) {
+        decode_e4m3_x4(in[0].x, out[0].x, out[0].y); decode_e4m3_x4(in[0].y, out[0].z, out[0].w);
+        decode_e4m3_x4(in[0].z, out[1].x, out[1].y); decode_e4m3_x4(in[0].w, out[1].z, out[1].w);
+    } else if constexpr (FMT == kE5M2) {
+        decode_e5m2_x4(in[0].x, out[0].x, out[0].y); decode_e5m2_x4(in[0].y, out[0].z, out[0].w);
+        decode_e5m2_x4(in[0].z, out[1].x, out[1].y); decode_e5m2_x4(in[0].w, out[1].z, out[1].w);
+    } else if constexpr (FMT == kE2M1U) {
+        decode_e2m1_unpacked_x4(in[0].x, out[0].x, out[0].y); decode_e2m1_unpacked_x4(in[0].y, out[0].z, out[0].w);
+        decode_e2m1_unpacked_x4(in[0].z, out[1].x, out[1].y); decode_e2m1_unpacked_x4(in[0].w, out[1].z, out[1].w);
+    } else if constexpr (FMT == kE2M1) {
+        uint32_t o[4];
+        decode_e2m1_packed_x8(in[0].x, o); out[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        decode_e2m1_packed_x8(in[0].y, o); out[1] = make_uint4(o[0], o[1], o[2], o[3]);
+        decode_e2m1_packed_x8(in[0].z, o); out[2] = make_uint4(o[0], o[1], o[2], o[3]);
+        decode_e2m1_packed_x8(in[0].w, o); out[3] = make_uint4(o[0], o[1], o[2], o[3]);
+    } else if constexpr (FMT == kBF16) {
+        out[0] = make_uint4(decode_bf16_x2(in[0].x), decode_bf16_x2(in[0].y), decode_bf16_x2(in[0].z),
+                            decode_bf16_x2(in[0].w));
+    } else if constexpr (FMT == kTF32) {
+        out[0] = make_uint4(decode_tf32_x2(in[0].x, in[0].y), decode_tf32_x2(in[0].z, in[0].w),
+                            decode_tf32_x2(in[1].x, in[1].y), decode_tf32_x2(in[1].z, in[1].w));
+    } else {
+        out[0] = in[0];
+    }
+}
+
+// Scalar decode of element i (used for tails and misaligned buffers).
+template <int FMT>
+__device__ __forceinline__ uint16_t decode_at(const void* src, size_t i) {
+    if constexpr (FMT == kE4M3) return tensor_bridge::e4m3_to_half_bits(static_cast<const uint8_t*>(src)[i]);
+    else if constexpr (FMT == kE5M2) return tensor_bridge::e5m2_to_half_bits(static_cast<const uint8_t*>(src)[i]);
+    else if constexpr (FMT == kE2M1U) return tensor_bridge::e2m1_to_half_bits(static_cast<const uint8_t*>(src)[i] & 0xFu);
+    else if constexpr (FMT == kE2M1) {
+        const uint8_t b = static_cast<const uint8_t*>(src)[i >> 1];
+        return tensor_bridge::e2m1_to_half_bits((i & 1) ? (b & 0xFu) : (b >> 4));
+    } else if constexpr (FMT == kBF16) return tensor_bridge::bf16_to_half_bits(static_cast<const uint16_t*>(src)[i]);
+    else if constexpr (FMT == kTF32) return tensor_bridge::tf32_to_half_bits(static_cast<const uint32_t*>(src)[i]);
+    else return static_cast<const uint16_t*>(src)[i];
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) k_decode_stream(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                       size_t units, const void* __restrict__ tail_src,
+                                                       uint16_t* __restrict__ tail_dst, size_t tail_begin,
+                                                       size_t n) {
+    using U = Unit<FMT>;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    size_t u = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    // Two units per thread per step: both loads are issued before either decode.
+    for (; u + stride < units; u += 2 * stride) {
+        uint4 a[U::kIn], b[U::kIn];
+#pragma unroll
+        for (int j = 0; j < U::kIn; ++j) a[j] = __ldcs(src + u * U::kIn + j);
+#pragma unroll
+        for (int j = 0; j < U::kIn; ++j) b[j] = __ldcs(src + (u + stride) * U::kIn + j);
+        uint4 oa[U::kOut], ob[U::kOut];
+        decode_vec<FMT>(a, oa);
+        decode_vec<FMT>(b, ob);
+#pragma unroll
+        for (int j = 0; j < U::kOut; ++j) dst[u * U::kOut + j] = oa[j];
+#pragma unroll
+        for (int j = 0; j < U::kOut; ++j) dst[(u + stride) * U::kOut + j] = ob[j];
+    }
+    if (u < units) {
+        uint4 a[U::kIn];
+#pragma unroll
+        for (int j = 0; j < U::kIn; ++j) a[j] = __ldcs(src + u * U::kIn + j);
+        uint4 oa[U::kOut];
+        decode_vec<FMT>(a, oa);
+#pragma unroll
+        for (int j = 0; j < U::kOut; ++j) dst[u * U::kOut + j] = oa[j];
+    }
+    // Elements past the last whole unit (fewer than one unit).
+    const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (tail_begin + gt < n) tail_dst[tail_begin + gt] = decode_at<FMT>(tail_src, tail_begin + gt);
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) k_decode_scalar(const void* __restrict__ src, uint16_t* __restrict__ dst,
+                                                       size_t n) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = decode_at<FMT>(src, i);
+}
+
+// src [rows x cols] -> dst [cols x rows].  Block = 256 threads handles a
+// 64-row x 32-column source tile: reads run along columns (contiguous in
+// src), writes along rows (contiguous in dst).
+template <int FMT>
+__global__ void __launch_bounds__(256) k_decode_transposed(const void* __restrict__ src, uint16_t* __restrict__ dst,
+                                                           int rows, int cols) {
+    __shared__ uint16_t tile[32][64 + 2];
+    const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int r = r0 + ty + 8 * k, c = c0 + tx;
+        if (r < rows && c < cols) tile[tx][ty + 8 * k] = decode_at<FMT>(src, static_cast<size_t>(r) * cols + c);
+    }
+    __syncthreads();
+    // Write: each warp writes 64 consecutive rows of one output row as 32 half2.
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int oc = ty + 8 * k;  // output row = source column c0 + oc
+        const int c = c0 + oc;
+        const int r = r0 + 2 * tx;
+        if (c < cols) {
+            uint16_t* out = dst + static_cast<size_t>(c) * rows + r;
+            if (r + 1 < rows && ((reinterpret_cast<uintptr_t>(out) & 3u) == 0)) {
+                *reinterpret_cast<uint32_t*>(out) =
+                    static_cast<uint32_t>(tile[oc][2 * tx]) | (static_cast<uint32_t>(tile[oc][2 * tx + 1]) << 16);
+            } else {
+                if (r < rows) out[0] = tile[oc][2 * tx];
+                if (r + 1 < rows) out[1] = tile[oc][2 * tx + 1];
+            }
+        }
+    }
+}
+
+// Nibble swap (reference FP4 packing <-> tensor-core packing).
+__global__ void __launch_bounds__(256) k_fp4_repack(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                    size_t n) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t n16 = n / 16;
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0;
+    size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (vec) {
+        for (size_t u = i; u < n16; u += stride) {
+            uint4 v = reinterpret_cast<const uint4*>(src)[u];
+            v.x = swap_nibbles(v.x); v.y = swap_nibbles(v.y); v.z = swap_nibbles(v.z); v.w = swap_nibbles(v.w);
+            reinterpret_cast<uint4*>(dst)[u] = v;
+        }
+        for (size_t k = n16 * 16 + i; k < n; k += stride) {
+            const uint8_t b = src[k];
+            dst[k] = static_cast<uint8_t>((b >> 4) | (b << 4));
+        }
+    } else {
+        for (size_t k = i; k < n; k += stride) {
+            const uint8_t b = src[k];
+            dst[k] = static_cast<uint8_t>((b >> 4) | (b << 4));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// Host launchers
+
+static size_t in_bytes_of(int fmt, size_t n) {
+    switch (fmt) {
+        case kE2M1: return (n + 1) / 2;
+        case kBF16: case kF16: return n * 2;
+        case kTF32: return n * 4;
+        default: return n;
+    }
+}
+
+template <int FMT>
+static cudaError_t launch_decode(const void* src, uint16_t* dst, size_t n, cudaStream_t st, int sms) {
+    using U = Unit<FMT>;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0;
+    if (!aligned) {
+        const size_t blocks = std::min<size_t>((n + 255) / 256, static_cast<size_t>(sms) * 8);
+        k_decode_scalar<FMT><<<static_cast<unsigned>(std::max<size_t>(blocks, 1)), 256, 0, st>>>(src, dst, n);
+        return cudaGetLastError();
+    }
+    const size_t units = n / U::kElems;
+    const size_t tail_begin = units * U::kElems;
+    const size_t want = (units + 255) / 256;
+    size_t blocks = std::min<size_t>(want, static_cast<size_t>(sms) * 8);
+    blocks = std::max<size_t>(blocks, 1);  // the tail needs at least one block (tail < 32 elements)
+    k_decode_stream<FMT><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+        static_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), units, src, dst, tail_begin, n);
+    return cudaGetLastError();
+}
+
+template <int FMT>
+static cudaError_t launch_decode_t(const void* src, uint16_t* dst, int rows, int cols, cudaStream_t st) {
+    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
+    k_decode_transposed<FMT><<<grid, 256, 0, st>>>(src, dst, rows, cols);
+    return cudaGetLastError();
+}
+
+cudaError_t decode_launch(int fmt, const void* src, uint16_t* dst, size_t n, cudaStream_t st, int sms) {
+    switch (fmt) {
+        case kF16: return launch_decode<kF16>(src, dst, n, st, sms);
+        case kE4M3: return launch_decode<kE4M3>(src, dst, n, st, sms);
+        case kE5M2: return launch_decode<kE5M2>(src, dst, n, st, sms);
+        case kE2M1: return launch_decode<kE2M1>(src, dst, n, st, sms);
+        case kE2M1U: return launch_decode<kE2M1U>(src, dst, n, st, sms);
+        case kBF16: return launch_decode<kBF16>(src, dst, n, st, sms);
+        case kTF32: return launch_decode<kTF32>(src, dst, n, st, sms);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t decode_transposed_launch(int fmt, const void* src, uint16_t* dst, int rows, int cols, cudaStream_t st) {
+    switch (fmt) {
+        case kF16: return launch_decode_t<kF16>(src, dst, rows, cols, st);
+        case kE4M3: return launch_decode_t<kE4M3>(src, dst, rows, cols, st);
+        case kE5M2: return launch_decode_t<kE5M2>(src, dst, rows, cols, st);
+        case kE2M1: return launch_decode_t<kE2M1>(src, dst, rows, cols, st);
+        case kE2M1U: return launch_decode_t<kE2M1U>(src, dst, rows, cols, st);
+        case kBF16: return launch_decode_t<kBF16>(src, dst, rows, cols, st);
+        case kTF32: return launch_decode_t<kTF32>(src, dst, rows, cols, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms) {
+    const size_t blocks = std::max<size_t>(1, std::min<size_t>((n / 16 + 255) / 256, static_cast<size_t>(sms) * 8));
+    k_fp4_repack<<<static_cast<unsigned>(blocks), 256, 0, st>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
+size_t stored_bytes(int fmt, size_t n) { return in_bytes_of(fmt, n); }
+
+}  // namespace tb

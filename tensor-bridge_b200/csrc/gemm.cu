@@ -1,0 +1,261 @@
+// gemm.cu -- instantiations and host-side planning of the tcgen05 GEMMs:
+// tile width, split-K, TMA tensor maps, launch.
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "gemm_kernel.cuh"
+#include "tb_host.h"
+
+namespace tb {
+
+cudaError_t device_error_read(int* v) { return cudaMemcpyFromSymbol(v, g_tb_device_error, sizeof(int)); }
+
+cudaError_t device_error_clear() {
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_tb_device_error, &zero, sizeof zero);
+}
+
+__global__ void k_splitk_reduce(const float* __restrict__ ws, void* D, long long ldd, int M, int N, int splits,
+                                float alpha, int out_f16) {
+    const size_t total = static_cast<size_t>(M) * N;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        float s = 0.0f;
+        for (int k = 0; k < splits; ++k) s += ws[static_cast<size_t>(k) * total + i];
+        const size_t r = i / N, c = i % N;
+        const size_t o = r * static_cast<size_t>(ldd) + c;
+        if (out_f16) static_cast<__half*>(D)[o] = __float2half_rn(s * alpha);
+        else static_cast<float*>(D)[o] = s * alpha;
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// Device info
+
+int current_device() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
+}
+
+const DeviceInfo& device_info(int dev) {
+    static DeviceInfo infos[64];
+    static std::once_flag flags[64];
+    dev = std::max(0, std::min(dev, 63));
+    std::call_once(flags[dev], [dev]() {
+        DeviceInfo& d = infos[dev];
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+        if (d.sms <= 0) d.sms = 148;
+    });
+    return infos[dev];
+}
+
+// ---------------------------------------------------------------------------------
+// TMA tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = []() -> EncodeTiledFn {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// Row-major 2-D map: `inner` elements per row (contiguous), `outer` rows,
+// `row_bytes` between rows; box of box_inner x box_outer elements.
+static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    std::memset(m, 0, sizeof(*m));
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------------
+// Configurations
+
+constexpr int kSmemBudget = 200 * 1024;
+
+template <int BN, int MODE, int FMT>
+struct Pick {
+    static constexpr int SD = MODE == kModeDecode ? (BN >= 128 ? 2 : 4) : 0;
+    static constexpr int RA = MODE == kModeDecode ? 128 * raw_row_bytes(FMT) : 128 * 128;
+    static constexpr int STAGE = RA + BN * 128;
+    static constexpr int SR0 = (kSmemBudget - SD * 128 * 128) / STAGE;
+    static constexpr int SR = SR0 > 12 ? 12 : (SR0 < 2 ? 2 : SR0);
+    using Cfg = GemmCfg<BN, MODE, FMT, SR, SD>;
+};
+
+template <class C>
+static cudaError_t launch_cfg(const CUtensorMap& ta, const CUtensorMap& tbm, const GemmArgs& args, cudaStream_t st,
+                              int dev) {
+    static std::atomic<uint64_t> attr_done{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_done.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
+        if (e != cudaSuccess) return e;
+        attr_done.fetch_or(bit);
+    }
+    const int sms = device_info(dev).sms;
+    const int grid = std::min(args.num_units, sms);
+    k_gemm<C><<<grid, C::NUM_THREADS, C::SMEM_ALLOC, st>>>(ta, tbm, args);
+    return cudaGetLastError();
+}
+
+static int choose_bn(int N) {
+    if (N <= 16) return 16;
+    if (N <= 64) return 64;
+    if (N <= 128) return 128;
+    return 256;
+}
+
+static int choose_splits(int units, int num_kb, int sms) {
+    if (units * 4 >= sms * 3) return 1;
+    int s = sms / std::max(units, 1);
+    s = std::min(s, 16);
+    s = std::min(s, std::max(1, num_kb / 4));
+    return std::max(s, 1);
+}
+
+static int kb_elems(GemmKind kind) { return kind == GemmKind::kNative ? 128 : 64; }
+
+size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int sms) {
+    (void)a_fmt;
+    if (M <= 0 || N <= 0 || K <= 0 || kind == GemmKind::kNative) return 0;
+    const int bn = choose_bn(N);
+    const int units = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    const int num_kb = (K + kb_elems(kind) - 1) / kb_elems(kind);
+    const int s = choose_splits(units, num_kb, sms);
+    if (s <= 1) return 0;
+    return static_cast<size_t>(s) * M * N * sizeof(float);
+}
+
+template <int BN, int MODE, int FMT>
+static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t st, int dev, const char** why) {
+    using C = typename Pick<BN, MODE, FMT>::Cfg;
+    CUtensorMap ta, tbm;
+    bool ok;
+    const uint64_t K = static_cast<uint64_t>(r.K);
+    if constexpr (MODE == kModeF16) {
+        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+        ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, BN,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+    } else if constexpr (MODE == kModeNative8) {
+        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+        ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.B, K, r.N, K, 128, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+        if constexpr (FMT == kE2M1) {
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K / 2, r.M, K / 2, 32, 128,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+        } else if constexpr (FMT == kBF16) {
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+        } else if constexpr (FMT == kTF32) {
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT32, r.A, K, r.M, K * 4, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+        } else {
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+        }
+        ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, BN,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (!ok) {
+        *why = "cuTensorMapEncodeTiled rejected the operand layout";
+        return cudaErrorInvalidValue;
+    }
+    return launch_cfg<C>(ta, tbm, args, st, dev);
+}
+
+template <int MODE, int FMT>
+static cudaError_t run_bn(int bn, const GemmRequest& r, const GemmArgs& a, cudaStream_t st, int dev, const char** why) {
+    switch (bn) {
+        case 16: return run<16, MODE, FMT>(r, a, st, dev, why);
+        case 64: return run<64, MODE, FMT>(r, a, st, dev, why);
+        case 128: return run<128, MODE, FMT>(r, a, st, dev, why);
+        case 256: return run<256, MODE, FMT>(r, a, st, dev, why);
+        default: *why = "unsupported tile width"; return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why) {
+    const int dev = current_device();
+    const int sms = device_info(dev).sms;
+    const int bn = r.force_bn ? r.force_bn : choose_bn(r.N);
+    const int tiles_m = (r.M + 127) / 128;
+    const int tiles_n = (r.N + bn - 1) / bn;
+    const int num_kb = (r.K + kb_elems(r.kind) - 1) / kb_elems(r.kind);
+    int splits = 1;
+    if (r.kind != GemmKind::kNative) {
+        splits = r.force_splits ? r.force_splits : choose_splits(tiles_m * tiles_n, num_kb, sms);
+        splits = std::max(1, std::min(splits, num_kb));
+    }
+    int kb_per = (num_kb + splits - 1) / splits;
+    splits = (num_kb + kb_per - 1) / kb_per;
+    if (splits > 1) {
+        const size_t need = static_cast<size_t>(splits) * r.M * r.N * sizeof(float);
+        if (r.workspace == nullptr || r.workspace_bytes < need) {
+            splits = 1;  // no room for partial sums: run unsplit
+            kb_per = num_kb;
+        }
+    }
+
+    GemmArgs a{};
+    a.M = r.M; a.N = r.N; a.K = r.K;
+    a.tiles_m = tiles_m; a.tiles_n = tiles_n; a.splits = splits;
+    a.kb_per_split = kb_per; a.num_kb = num_kb;
+    a.num_units = tiles_m * tiles_n * splits;
+    a.alpha = r.alpha;
+    a.D = r.D; a.ldd = r.ldd;
+    a.out_f16 = r.out_f16;
+    const int vec_elems = r.out_f16 ? 8 : 4;
+    a.vec_ok = ((reinterpret_cast<uintptr_t>(r.D) & 15u) == 0 && (r.ldd % vec_elems) == 0) ? 1 : 0;
+    a.ws = splits > 1 ? static_cast<float*>(r.workspace) : nullptr;
+
+    cudaError_t e;
+    switch (r.kind) {
+        case GemmKind::kF16: e = run_bn<kModeF16, kF16>(bn, r, a, st, dev, why); break;
+        case GemmKind::kNative:
+            if (r.a_fmt != kE4M3) { *why = "native GEMM supports E4M3 x E4M3"; return cudaErrorInvalidValue; }
+            if (bn == 16) e = run<16, kModeNative8, kE4M3>(r, a, st, dev, why);
+            else if (bn == 64) e = run<64, kModeNative8, kE4M3>(r, a, st, dev, why);
+            else if (bn == 128) e = run<128, kModeNative8, kE4M3>(r, a, st, dev, why);
+            else e = run<256, kModeNative8, kE4M3>(r, a, st, dev, why);
+            break;
+        case GemmKind::kFused:
+            switch (r.a_fmt) {
+                case kE4M3: e = run_bn<kModeDecode, kE4M3>(bn, r, a, st, dev, why); break;
+                case kE5M2: e = run_bn<kModeDecode, kE5M2>(bn, r, a, st, dev, why); break;
+                case kE2M1: e = run_bn<kModeDecode, kE2M1>(bn, r, a, st, dev, why); break;
+                case kE2M1U: e = run_bn<kModeDecode, kE2M1U>(bn, r, a, st, dev, why); break;
+                case kBF16: e = run_bn<kModeDecode, kBF16>(bn, r, a, st, dev, why); break;
+                case kTF32: e = run_bn<kModeDecode, kTF32>(bn, r, a, st, dev, why); break;
+                case kF16: e = run_bn<kModeF16, kF16>(bn, r, a, st, dev, why); break;
+                default: *why = "unsupported weight format"; return cudaErrorInvalidValue;
+            }
+            break;
+        default: *why = "unknown GEMM kind"; return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess || splits <= 1) return e;
+    const size_t total = static_cast<size_t>(r.M) * r.N;
+    const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, static_cast<size_t>(sms) * 8));
+    k_splitk_reduce<<<std::max(blocks, 1), 256, 0, st>>>(a.ws, r.D, r.ldd, r.M, r.N, splits, r.alpha, r.out_f16);
+    return cudaGetLastError();
+}
+
+}  // namespace tb

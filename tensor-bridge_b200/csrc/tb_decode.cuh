@@ -1,0 +1,161 @@
+// tb_decode.cuh -- vectorised, bit-exact decoders from the stored formats to
+// FP16, used by the streaming decode kernels and by the decode warps of the
+// fused GEMM.  Every function reproduces the reference primitive of its format
+// (include/tensor_bridge/{fp8,fp4,bf16,tf32}.h of tensor-bridge) on every
+// input bit pattern; the exhaustive decode tests compare them code by code.
+//
+// Output packing: a uint32_t holds two FP16 values, the lower-addressed
+// (earlier) element in the low 16 bits, so words can be stored as-is.
+#pragma once
+
+#include <cstdint>
+#include "tensor_bridge/fp8.h"
+#include "tensor_bridge/fp4.h"
+#include "tensor_bridge/bf16.h"
+#include "tensor_bridge/tf32.h"
+
+namespace tb {
+
+// prmt.b32 in its default mode.  Each selector nibble picks byte [2:0] of the
+// pair {b, a} (a = bytes 0-3); if bit 3 of the nibble is set the byte's sign
+// bit is replicated instead (0x00 or 0xFF).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// Two E4M3 codes (low byte = first) -> two FP16 values by the hardware
+// converter.  Exact for every code whose exponent field is non-zero and that
+// is not a NaN; the callers route the other codes through the scalar path.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(uint16_t pair) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(pair));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) {
+    return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// ---- E4M3 --------------------------------------------------------------------------
+
+// Bit 7 of each byte set where the E4M3 code needs the scalar path: exponent
+// field 0 with a non-zero mantissa (a subnormal, flushed by the reference) or
+// magnitude 0x7F (NaN, which the reference encodes as 0x7E00).
+__device__ __forceinline__ uint32_t e4m3_special_mask(uint32_t w) {
+    const uint32_t mag = w & 0x7F7F7F7Fu;
+    const uint32_t is_nan = mag + 0x01010101u;                 // bit 7 iff mag == 0x7F
+    const uint32_t exp_nz = mag + 0x78787878u;                 // bit 7 iff exponent != 0
+    const uint32_t man_nz = ((w & 0x07070707u) + 0x07070707u) << 4;  // bit 7 iff mantissa != 0
+    return (is_nan | (man_nz & ~exp_nz)) & 0x80808080u;
+}
+
+// Four E4M3 codes (byte 0 first) -> four FP16 values in o[0..1].
+__device__ __forceinline__ void decode_e4m3_x4(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    if (e4m3_special_mask(w) == 0u) {
+        o0 = cvt_e4m3x2(static_cast<uint16_t>(w & 0xFFFFu));
+        o1 = cvt_e4m3x2(static_cast<uint16_t>(w >> 16));
+    } else {
+        using tensor_bridge::e4m3_to_half_bits;
+        o0 = pack2(e4m3_to_half_bits(w & 0xFFu), e4m3_to_half_bits((w >> 8) & 0xFFu));
+        o1 = pack2(e4m3_to_half_bits((w >> 16) & 0xFFu), e4m3_to_half_bits(w >> 24));
+    }
+}
+
+// ---- E5M2: each code is the top byte of its FP16 value -------------------------------
+
+__device__ __forceinline__ void decode_e5m2_x4(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    o0 = prmt(w, 0u, 0x1404u);  // bytes {0, b0, 0, b1}
+    o1 = prmt(w, 0u, 0x3424u);  // bytes {0, b2, 0, b3}
+}
+
+// ---- E2M1 ----------------------------------------------------------------------------
+// All 16 E2M1 values have FP16 encodings with a zero low byte, so the decode is
+// a byte table lookup on the 3-bit magnitude (one prmt over two constant words)
+// plus the sign bit.  High bytes for magnitudes 0..7:
+//   0x00 0x38 0x3C 0x3E | 0x40 0x42 0x44 0x46
+constexpr uint32_t kE2M1HiLo = 0x3E3C3800u;
+constexpr uint32_t kE2M1HiHi = 0x46444240u;
+
+// Packed, reference order: byte j holds element 2j in its HIGH nibble and
+// element 2j+1 in its low nibble.  Eight elements -> o[0..3].
+__device__ __forceinline__ void decode_e2m1_packed_x8(uint32_t w, uint32_t (&o)[4]) {
+    const uint32_t mag = w & 0x77777777u;  // nibble k = magnitude of nibble k
+    // Byte k of hb0/hb1 = high FP16 byte of nibble k (k = 0..3 / 4..7).
+    const uint32_t hb0 = prmt(kE2M1HiLo, kE2M1HiHi, mag);
+    const uint32_t hb1 = prmt(kE2M1HiLo, kE2M1HiHi, mag >> 16);
+    // Sign of nibble k sits in bit 4k+3.  Odd nibbles (high halves of bytes)
+    // have it in a byte's bit 7; even nibbles after a 4-bit left shift.
+    const uint32_t ws = w << 4;
+    const uint32_t s0 = prmt(ws, w, 0xD9C8u);  // nibbles 0,1,2,3 -> 0x00/0xFF
+    const uint32_t s1 = prmt(ws, w, 0xFBEAu);  // nibbles 4,5,6,7
+    const uint32_t v0 = hb0 | (s0 & 0x80808080u);
+    const uint32_t v1 = hb1 | (s1 & 0x80808080u);
+    // Element order: e0 = nibble 1, e1 = nibble 0, e2 = nibble 3, e3 = nibble 2 ...
+    o[0] = prmt(v0, 0u, 0x0414u);  // {0, nib1, 0, nib0}
+    o[1] = prmt(v0, 0u, 0x2434u);  // {0, nib3, 0, nib2}
+    o[2] = prmt(v1, 0u, 0x0414u);
+    o[3] = prmt(v1, 0u, 0x2434u);
+}
+
+// Unpacked (one value per byte, low nibble; high nibble ignored as in the
+// reference's `nibble & 0x0F`).  Four elements -> o0, o1.
+__device__ __forceinline__ void decode_e2m1_unpacked_x4(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    const uint32_t mag = w & 0x07070707u;
+    const uint32_t sel = prmt(mag | (mag >> 4), 0u, 0x4420u);  // nibbles = magnitudes of bytes 0..3
+    const uint32_t hb = prmt(kE2M1HiLo, kE2M1HiHi, sel);
+    const uint32_t v = hb | ((w << 4) & 0x80808080u);         // bit 3 of each byte -> bit 7
+    o0 = prmt(v, 0u, 0x1404u);
+    o1 = prmt(v, 0u, 0x3424u);
+}
+
+// Tensor-core packing (element 2j in the LOW nibble): a nibble swap of the
+// reference order.
+__device__ __forceinline__ uint32_t swap_nibbles(uint32_t w) {
+    return ((w >> 4) & 0x0F0F0F0Fu) | ((w << 4) & 0xF0F0F0F0u);
+}
+
+// ---- BF16 ---------------------------------------------------------------------------
+
+// Lane mask from bit 15 of each 16-bit lane: 0xFFFF where set.
+__device__ __forceinline__ uint32_t lane_mask_bit15(uint32_t x) { return prmt(x, 0u, 0xBB99u); }
+
+// Two BF16 values (low lane first) -> two FP16 values.  Fast path: widen to
+// FP32 (exact), convert with the hardware FP32->FP16x2 converter (exact for
+// BF16 values in FP16 range, Inf beyond, as the reference), then flush FP16
+// subnormal results to a signed zero (the reference maps every BF16 value
+// below 2^-14 to zero; no BF16 value below 2^-14 rounds up to 2^-14).  BF16
+// NaN lanes take the scalar path (the reference encodes them as 0x7E00).
+__device__ __forceinline__ uint32_t decode_bf16_x2(uint32_t w) {
+    const uint32_t nan_lanes = ((w & 0x7FFF7FFFu) + 0x007F007Fu) & 0x80008000u;
+    if (nan_lanes != 0u) {
+        return pack2(tensor_bridge::bf16_to_half_bits(w & 0xFFFFu), tensor_bridge::bf16_to_half_bits(w >> 16));
+    }
+    const float lo = __uint_as_float(w << 16);
+    const float hi = __uint_as_float(w & 0xFFFF0000u);
+    uint32_t h;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+    const uint32_t normal = lane_mask_bit15((h & 0x7C007C00u) + 0x7C007C00u);
+    return h & (normal | 0x80008000u);
+}
+
+// ---- TF32 ---------------------------------------------------------------------------
+
+// One TF32 word -> FP16 bits, the reference rule (tf32.h:22-34) written with
+// selects: re-biased exponent <= 0 -> signed zero, >= 31 -> Inf or NaN.
+__device__ __forceinline__ uint32_t decode_tf32_x1(uint32_t t) {
+    const uint32_t s = (t >> 16) & 0x8000u;
+    const uint32_t mag = t & 0x7FFFFFFFu;
+    uint32_t h = (mag >> 13) - (112u << 10);          // valid when 113 <= exp <= 142
+    h = mag < (113u << 23) ? 0u : h;                  // exponent - 112 <= 0
+    const uint32_t big = mag > 0x7F800000u ? 0x7E00u : 0x7C00u;
+    h = mag >= (143u << 23) ? big : h;                // exponent - 112 >= 31
+    return s | h;
+}
+
+__device__ __forceinline__ uint32_t decode_tf32_x2(uint32_t t0, uint32_t t1) {
+    return decode_tf32_x1(t0) | (decode_tf32_x1(t1) << 16);
+}
+
+}  // namespace tb

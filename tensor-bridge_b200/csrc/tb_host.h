@@ -1,0 +1,55 @@
+// tb_host.h -- internal host-side declarations shared by the .cu files.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace tb {
+
+// decode.cu
+cudaError_t decode_launch(int fmt, const void* src, uint16_t* dst, size_t n, cudaStream_t st, int sms);
+cudaError_t decode_transposed_launch(int fmt, const void* src, uint16_t* dst, int rows, int cols, cudaStream_t st);
+cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms);
+size_t stored_bytes(int fmt, size_t n);
+
+// gemm.cu
+enum class GemmKind { kF16, kFused, kNative };
+
+struct GemmRequest {
+    GemmKind kind;
+    int a_fmt;          // stored format of A (decode / native) or kF16
+    const void* A;
+    const void* B;      // FP16 [N x K] (f16 / fused) or E4M3 [N x K] (native)
+    void* D;
+    long long ldd;      // row stride of D in elements (normally N)
+    int M, N, K;
+    int out_f16;
+    float alpha;
+    void* workspace;
+    size_t workspace_bytes;
+    int force_bn;       // 0 = choose automatically (for tests and tuning)
+    int force_splits;   // 0 = choose automatically
+};
+
+// Split-K workspace needed by a fused/f16 GEMM of this shape (0 if none).
+size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int sms);
+
+// Validated launch.  Returns cudaSuccess or the failing CUDA error; sets
+// *why to a static message when the request itself is unsupported.
+cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why);
+
+// Device error word of the GEMM kernels (bounded-wait expiry).
+cudaError_t device_error_read(int* v);
+cudaError_t device_error_clear();
+
+// Device properties cached per device.
+struct DeviceInfo {
+    int sms;
+    int major, minor;
+};
+const DeviceInfo& device_info(int dev);
+int current_device();
+
+}  // namespace tb

@@ -1,0 +1,164 @@
+"""tcgen05 GEMMs on the GPU against the oracle (decode -> FP16 -> FP32 sums).
+
+Tolerance: relative Frobenius error <= 1e-3 against the oracle on the same
+inputs (the bound the decode+GEMM path is held to); both sides compute exact
+FP32 products of FP16 values and differ only in summation order, so the
+observed errors are ~1e-6.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from gpu_util import to_dev, empty_dev, from_dev
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def make_operands(fmt, M, N, K, seed=0, dist="normal"):
+    """Weight A [M x K] quantized to fmt with a per-tensor scale, activations
+    B [N x K] FP16.  Returns (A stored, B16 bits, alpha = 1/scale)."""
+    if dist == "normal":
+        a = O.normal(seed, (M, K), 0.02)
+        b = O.normal(seed + 1, (N, K), 1.0)
+    else:
+        a = O.uniform(seed, (M, K))
+        b = O.uniform(seed + 1, (N, K))
+    s = O.per_tensor_scale(a, fmt)
+    A = O.quantize(fmt, a, s) if fmt != O.F16 else O.f32_to_f16_bits(a).reshape(M, K)
+    B16 = O.f32_to_f16_bits(b).reshape(N, K)
+    return A, B16, float(np.float32(1.0) / np.float32(s))
+
+
+def run_fused(tb, torch, fmt, A, B16, M, N, K, alpha, out=None, force_ws=True):
+    out = out if out is not None else tb.Out.F32
+    dA, dB = to_dev(torch, A), to_dev(torch, B16)
+    esz = 2 if out == tb.Out.F16 else 4
+    dD = empty_dev(torch, M * N * esz + 256)
+    ws_bytes = tb.fused_workspace_bytes(fmt, M, N, K) if force_ws else 0
+    ws = empty_dev(torch, ws_bytes) if ws_bytes else None
+    tb.gemm_fused(fmt, dA, dB, dD, M, N, K, out=out, alpha=alpha, workspace=ws, workspace_bytes=ws_bytes)
+    torch.cuda.synchronize()
+    raw = from_dev(dD, np.uint8)
+    assert np.all(raw[M * N * esz:] == 0xA5), "wrote past the end of D"
+    body = raw[: M * N * esz]
+    if out == tb.Out.F16:
+        return O.f16_bits_to_f32(body.view(np.uint16)).reshape(M, N)
+    return body.view(np.float32).reshape(M, N)
+
+
+def check(got, want, tol=TOL):
+    err = O.rel_frob(got, want)
+    assert np.all(np.isfinite(got)), "non-finite outputs"
+    assert err <= tol, f"rel-Frobenius {err:.3e} > {tol}"
+    return err
+
+
+SHAPES = [
+    (256, 256, 256),     # the 256^3 configuration
+    (128, 256, 64),      # one tile, one k-block
+    (200, 72, 48),       # ragged M/N, K not a multiple of 64
+    (384, 520, 320),     # several tiles, ragged N
+    (1000, 1, 512),      # one token
+    (640, 16, 1024),     # 16 tokens
+    (512, 128, 4096),    # 128 tokens, long K (split-K candidates)
+    (130, 300, 96),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_f16(tb, cuda, M, N, K):
+    A, B16, _ = make_operands(O.F16, M, N, K, seed=M + N + K, dist="uniform")
+    dA, dB = to_dev(cuda, A), to_dev(cuda, B16)
+    dD = empty_dev(cuda, M * N * 4)
+    tb.gemm_f16(dA, dB, dD, M, N, K)
+    cuda.cuda.synchronize()
+    got = from_dev(dD, np.float32).reshape(M, N)
+    check(got, O.gemm(O.F16, A, O.F16, B16, M, N, K))
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E5M2, O.E2M1, O.E2M1_UNPACKED, O.BF16, O.TF32])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_fused(tb, cuda, fmt, M, N, K):
+    if fmt == O.E2M1 and K % 32:
+        pytest.skip("packed FP4 needs K % 32 == 0")
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=fmt * 7 + M)
+    got = run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha)
+    check(got, O.gemm(fmt, A, O.F16, B16, M, N, K, alpha=alpha))
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
+def test_gemm_fused_f16_out(tb, cuda, fmt):
+    M, N, K = 384, 264, 512
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=3)
+    got = run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha, out=tb.Out.F16)
+    want = O.f16_bits_to_f32(O.gemm(fmt, A, O.F16, B16, M, N, K, alpha=alpha, out_f16=True))
+    check(got, want)
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1])
+def test_gemm_fused_without_workspace(tb, cuda, fmt):
+    """Short-and-wide shapes split K when given a workspace and still run
+    (unsplit) without one; both agree with the oracle."""
+    M, N, K = 256, 16, 8192
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=4)
+    assert tb.fused_workspace_bytes(fmt, M, N, K) > 0
+    want = O.gemm(fmt, A, O.F16, B16, M, N, K, alpha=alpha)
+    check(run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha, force_ws=True), want)
+    check(run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha, force_ws=False), want)
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1, O.BF16, O.TF32])
+def test_fused_equals_unfused_bitwise(tb, cuda, fmt):
+    """Decode-in-shared-memory and decode-kernel-then-GEMM run the same MMAs in
+    the same order: identical bits (the reference checks the same property,
+    bench/bench_fused.cu:85-87)."""
+    M, N, K = 512, 384, 1024
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=6)
+    fused = run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha, force_ws=False)
+    dA, dB = to_dev(cuda, A), to_dev(cuda, B16)
+    A16 = empty_dev(cuda, M * K * 2)
+    tb.decode(fmt, dA, A16, M * K)
+    dD = empty_dev(cuda, M * N * 4)
+    tb.gemm_f16(A16, dB, dD, M, N, K, alpha=alpha)
+    cuda.cuda.synchronize()
+    unfused = from_dev(dD, np.float32).reshape(M, N)
+    np.testing.assert_array_equal(fused.view(np.uint32), unfused.view(np.uint32))
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (384, 200, 640), (128, 16, 2048)])
+def test_gemm_native_e4m3(tb, cuda, M, N, K):
+    a = O.normal(10, (M, K), 0.02)
+    b = O.normal(11, (N, K), 1.0)
+    sa, sb = O.per_tensor_scale(a, O.E4M3), O.per_tensor_scale(b, O.E4M3)
+    A, B = O.quantize(O.E4M3, a, sa), O.quantize(O.E4M3, b, sb)
+    alpha = float(np.float32(1.0) / (np.float32(sa) * np.float32(sb)))
+    dA, dB = to_dev(cuda, A), to_dev(cuda, B)
+    dD = empty_dev(cuda, M * N * 4)
+    tb.gemm_native(tb.Format.E4M3, dA, tb.Format.E4M3, dB, dD, M, N, K, alpha=alpha)
+    cuda.cuda.synchronize()
+    got = from_dev(dD, np.float32).reshape(M, N)
+    check(got, O.gemm(O.E4M3, A, O.E4M3, B, M, N, K, alpha=alpha))
+
+
+def test_fp8_fused_fp16_mirror(tb, cuda):
+    """tb_gemm_fp8_fused_fp16 mirrors gemm_fp8_fused_fp16: both operands E4M3,
+    B given [K x N] row-major as the reference reads it."""
+    M, N, K = 512, 512, 512
+    a, b = O.uniform(20, (M, K)), O.uniform(21, (K, N))
+    A, Bkn = O.quantize(O.E4M3, a), O.quantize(O.E4M3, b)
+    dA, dB = to_dev(cuda, A), to_dev(cuda, Bkn)
+    ws_bytes = tb.lib().tb_gemm_fp8_fused_workspace(M, N, K)
+    ws = empty_dev(cuda, ws_bytes)
+    dD = empty_dev(cuda, M * N * 4)
+    tb.call("tb_gemm_fp8_fused_fp16", dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), M, N, K, ws.data_ptr(), ws_bytes,
+            cuda.cuda.current_stream().cuda_stream)
+    cuda.cuda.synchronize()
+    got = from_dev(dD, np.float32).reshape(M, N)
+    Bnk = np.ascontiguousarray(Bkn.reshape(K, N).T)
+    check(got, O.gemm(O.E4M3, A, O.E4M3, Bnk, M, N, K))
+
+
+def test_no_device_error_word(tb, cuda):
+    assert tb.device_error(clear=True) == 0
