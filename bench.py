@@ -1,0 +1,550 @@
+#!/usr/bin/env python
+"""bench.py -- decode + GEMM throughput of the B200 path.
+
+Default workload (one GPU): the format sweep at M = N = K = 4096.  One step is,
+for each stored weight format TF32, BF16, FP8 E4M3 and FP4 E2M1 (A = weights
+drawn from N(0, 0.02), per-tensor scale FORMAT_MAX/maxabs for FP8/FP4, B =
+FP16 activations from N(0, 1)):
+    * the fused decode-in-shared-memory GEMM  D = alpha * decode(A) @ B^T
+    * the unfused path: decode kernel to FP16 in HBM, then the tcgen05 GEMM
+and once the both-quantized case qA @ qB with E4M3 x E4M3 on the native
+kind::f8f6f4 tensor-core path; FP32 output, as the reference.  That is 9
+GEMMs of 2*4096^3 flops per step.  `value` is whole-job TFLOP/s.
+
+On N GPUs (torchrun) every rank runs the same sweep on its own data (the
+sweep has no exchange step): weak scaling, value = all ranks' flops / the
+slowest rank's time.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "decode+GEMM TFLOPS (% tcgen05 peak) and GB/s (% HBM) per format; rel-Frob err"
+UNIT = "TFLOP/s"
+FORMATS = ["tf32", "bf16", "e4m3", "e2m1"]
+FORMAT_MAX = {"e4m3": 448.0, "e2m1": 6.0}
+
+
+def load_package():
+    name = "tensor_bridge_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg_dir = os.path.join(ROOT, "tensor-bridge_b200")
+    spec = importlib.util.spec_from_file_location(name, os.path.join(pkg_dir, "__init__.py"),
+                                                  submodule_search_locations=[pkg_dir])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---- clocks sampled during the timed region ------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, cuda_index: int):
+        # nvidia-smi numbers GPUs physically; map through CUDA_VISIBLE_DEVICES.
+        vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        self.gpu = vis[cuda_index].strip() if cuda_index < len(vis) else str(cuda_index)
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---- distributed plumbing ------------------------------------------------------------------
+
+class Dist:
+    def __init__(self, torch, want_gpus: int):
+        self.torch = torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dist = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+        else:
+            torch.cuda.set_device(0)
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.dist:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.dist:
+            self.dist.destroy_process_group()
+
+
+# ---- the format sweep ----------------------------------------------------------------------
+
+class Sweep:
+    def __init__(self, torch, tb, M: int, N: int, K: int, seed: int):
+        self.torch, self.tb = torch, tb
+        self.M, self.N, self.K = M, N, K
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        F = tb.Format
+        self.fmt = {"tf32": F.TF32, "bf16": F.BF16, "e4m3": F.E4M3, "e2m1": F.E2M1}
+        self.a32 = {}
+        self.Aq, self.alpha = {}, {}
+        amax = torch.zeros(1, dtype=torch.float32, device=dev)
+        for i, name in enumerate(FORMATS):
+            a = torch.randn(M, K, generator=g, device=dev) * 0.02
+            scale = 1.0
+            if name in FORMAT_MAX:
+                tb.absmax(a, a.numel(), amax)
+                m = float(amax.item())
+                scale = float(np.float32(FORMAT_MAX[name]) / np.float32(m if m > 0 else 1.0))
+            f = self.fmt[name]
+            q = torch.empty(tb.stored_bytes(f, M * K), dtype=torch.uint8, device=dev)
+            tb.quantize(f, a, q, M * K, scale=scale)
+            self.Aq[name] = q
+            self.a32[name] = a
+            self.alpha[name] = float(np.float32(1.0) / np.float32(scale))
+        b = torch.randn(N, K, generator=g, device=dev)
+        self.b32 = b
+        self.B16 = torch.empty(N * K * 2, dtype=torch.uint8, device=dev)
+        tb.quantize(F.F16, b, self.B16, N * K)
+        # both-quantized case: B to E4M3 with its own per-tensor scale
+        tb.absmax(b, b.numel(), amax)
+        sb = float(np.float32(448.0) / np.float32(float(amax.item())))
+        self.B8 = torch.empty(N * K, dtype=torch.uint8, device=dev)
+        tb.quantize(F.E4M3, b, self.B8, N * K, scale=sb)
+        self.alpha_native = float(np.float32(1.0) / (np.float32(1.0 / self.alpha["e4m3"]) * np.float32(sb)))
+        self.A16 = torch.empty(M * K * 2, dtype=torch.uint8, device=dev)
+        self.Dfused = {n: torch.empty(M, N, dtype=torch.float32, device=dev) for n in FORMATS}
+        self.Dunf = torch.empty(M, N, dtype=torch.float32, device=dev)
+        self.Dnat = torch.empty(M, N, dtype=torch.float32, device=dev)
+        self.flops_per_gemm = 2.0 * M * N * K
+        self.launches = 0
+
+    # The GEMMs of one step, each as (label, callable).
+    def ops(self):
+        tb, M, N, K = self.tb, self.M, self.N, self.K
+        out = []
+        for name in FORMATS:
+            f, A, al = self.fmt[name], self.Aq[name], self.alpha[name]
+            out.append((f"fused_{name}", lambda f=f, A=A, al=al, name=name: tb.gemm_fused(
+                f, A, self.B16, self.Dfused[name], M, N, K, out=tb.Out.F32, alpha=al)))
+            out.append((f"decode_{name}", lambda f=f, A=A: tb.decode(f, A, self.A16, M * K)))
+            out.append((f"gemm_after_{name}", lambda al=al: tb.gemm_f16(self.A16, self.B16, self.Dunf, M, N, K,
+                                                                        out=tb.Out.F32, alpha=al)))
+        out.append(("native_e4m3", lambda: tb.gemm_native(tb.Format.E4M3, self.Aq["e4m3"], tb.Format.E4M3, self.B8,
+                                                          self.Dnat, M, N, K, out=tb.Out.F32,
+                                                          alpha=self.alpha_native)))
+        return out
+
+    def gemm_flops(self, label: str) -> float:
+        return 0.0 if label.startswith("decode_") else self.flops_per_gemm
+
+    def step_flops(self) -> float:
+        return sum(self.gemm_flops(l) for l, _ in self.ops())
+
+    def decode_bytes(self, name: str) -> int:
+        return self.Aq[name].numel() + self.M * self.K * 2
+
+
+def flush_l2(torch, buf):
+    buf.add_(1)  # read + write 256 MiB, larger than the 126 MB L2
+
+
+def run_device(torch, tb, sw: Sweep, steps: int, warmup: int, dist: Dist):
+    ops = sw.ops()
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    for _ in range(warmup):
+        flush_l2(torch, flush)
+        for _, fn in ops:
+            fn()
+    torch.cuda.synchronize()
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops]
+          for _ in range(steps)]
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    time.sleep(0.3)
+    dist.barrier()
+    torch.cuda.synchronize()
+    launches = 0
+    for s in range(steps):
+        flush_l2(torch, flush)  # between timed steps, outside the events
+        for j, (_, fn) in enumerate(ops):
+            ev[s][j][0].record(stream)
+            fn()
+            ev[s][j][1].record(stream)
+            launches += 1
+    torch.cuda.synchronize()
+    dist.barrier()
+    clock = clocks.stop()
+    per_op = {}
+    total_ms = 0.0
+    for s in range(steps):
+        for j, (label, _) in enumerate(ops):
+            ms = ev[s][j][0].elapsed_time(ev[s][j][1])
+            per_op.setdefault(label, []).append(ms)
+            total_ms += ms
+    return total_ms, per_op, launches, clock
+
+
+def run_e2e(torch, tb, sw: Sweep, steps: int, warmup: int):
+    """The same GEMMs through the C ABI with host inputs and outputs: every
+    GEMM copies its operands from pinned host memory, runs, and copies D back."""
+    M, N, K = sw.M, sw.N, sw.K
+    hA = {n: sw.Aq[n].cpu().pin_memory() for n in FORMATS}
+    hB16 = sw.B16.cpu().pin_memory()
+    hB8 = sw.B8.cpu().pin_memory()
+    hD = torch.empty(M, N, dtype=torch.float32).pin_memory()
+    dA = torch.empty(max(a.numel() for a in sw.Aq.values()), dtype=torch.uint8, device="cuda")
+    dB = torch.empty(sw.B16.numel(), dtype=torch.uint8, device="cuda")
+    dB8 = torch.empty(sw.B8.numel(), dtype=torch.uint8, device="cuda")
+    h2d = d2h = 0
+
+    def step():
+        nonlocal h2d, d2h
+        h2d = d2h = 0
+        for name in FORMATS:
+            f, al = sw.fmt[name], sw.alpha[name]
+            n = hA[name].numel()
+            dA[:n].copy_(hA[name], non_blocking=True)
+            dB.copy_(hB16, non_blocking=True)
+            tb.gemm_fused(f, dA, dB, sw.Dunf, M, N, K, out=tb.Out.F32, alpha=al)
+            hD.copy_(sw.Dunf, non_blocking=True)
+            dA[:n].copy_(hA[name], non_blocking=True)
+            dB.copy_(hB16, non_blocking=True)
+            tb.decode(f, dA, sw.A16, M * K)
+            tb.gemm_f16(sw.A16, dB, sw.Dunf, M, N, K, out=tb.Out.F32, alpha=al)
+            hD.copy_(sw.Dunf, non_blocking=True)
+            h2d += 2 * (n + hB16.numel())
+            d2h += 2 * hD.numel() * 4
+        n = hA["e4m3"].numel()
+        dA[:n].copy_(hA["e4m3"], non_blocking=True)
+        dB8.copy_(hB8, non_blocking=True)
+        tb.gemm_native(tb.Format.E4M3, dA, tb.Format.E4M3, dB8, sw.Dnat, M, N, K, out=tb.Out.F32,
+                       alpha=sw.alpha_native)
+        hD.copy_(sw.Dnat, non_blocking=True)
+        h2d += n + hB8.numel()
+        d2h += hD.numel() * 4
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    return ms, h2d, d2h
+
+
+def quality(torch, tb, sw: Sweep, rows: int = 256):
+    """rel-Frobenius error of the fused result against the unquantized FP32
+    product (the reference's err measure, bench/bench_formats.cu:97-103), on
+    `rows` sampled rows; and whether fused == unfused bitwise."""
+    out = {}
+    r = torch.arange(0, sw.M, max(1, sw.M // rows), device="cuda")[:rows]
+    ref = sw.a32  # fp32 originals
+    for name in FORMATS:
+        want = ref[name][r].double() @ sw.b32.double().T
+        got = sw.Dfused[name][r].double()
+        err = float(torch.linalg.norm(got - want) / torch.linalg.norm(want))
+        # unfused result for the same format, recomputed here for the bitwise check
+        tb.decode(sw.fmt[name], sw.Aq[name], sw.A16, sw.M * sw.K)
+        tb.gemm_f16(sw.A16, sw.B16, sw.Dunf, sw.M, sw.N, sw.K, out=tb.Out.F32, alpha=sw.alpha[name])
+        torch.cuda.synchronize()
+        same = bool(torch.equal(sw.Dfused[name].view(torch.int32), sw.Dunf.view(torch.int32)))
+        out[name] = {"rel_frob_vs_fp32": err, "fused_equals_unfused": same}
+    want = ref["e4m3"][r].double() @ sw.b32.double().T
+    out["native_e4m3"] = {"rel_frob_vs_fp32": float(torch.linalg.norm(sw.Dnat[r].double() - want) /
+                                                    torch.linalg.norm(want))}
+    return out
+
+
+# ---- CPU baseline: the reference's own host path ---------------------------------------
+
+def cpu_baseline(sw_shape, seconds: float = 12.0):
+    """Time tensor-bridge's host decode primitives + its FP32 GEMM loop
+    (oracle/_ref, compiled from the reference headers) on a row sample of the
+    sweep, on all host threads.  Falls back to the oracle port if _ref is absent."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    M, N, K = sw_shape
+    threads = host_threads()
+    fmts = {"tf32": O.TF32, "bf16": O.BF16, "e4m3": O.E4M3, "e2m1": O.E2M1}
+    rng_rows = 32
+    data = {}
+    b = O.normal(1, (N, K), 1.0)
+    B16 = O.f32_to_f16_bits(b).reshape(N, K)
+    for name, f in fmts.items():
+        a = O.normal(2, (rng_rows * 64, K), 0.02)
+        s = O.per_tensor_scale(a, f)
+        data[name] = (f, O.quantize(f, a, s), float(np.float32(1) / np.float32(s)))
+    use_ref = O.ref_lib() is not None
+    run = (lambda f, A, al, rows: O.ref_cpu_gemm(f, A, B16, A.shape[0], N, K, rows=rows, alpha=al,
+                                                 threads=threads)) if use_ref else \
+          (lambda f, A, al, rows: O.gemm(f, A, O.F16, B16, A.shape[0], N, K, rows=rows, alpha=al,
+                                         threads=threads))
+    # calibrate: rows per format so the whole sample takes about `seconds`
+    t0 = time.perf_counter()
+    for f, A, al in data.values():
+        run(f, A, al, (0, threads))
+    per_row = (time.perf_counter() - t0) / (threads * len(data))
+    rows = max(threads, int(seconds / (per_row * len(data))) // threads * threads)
+    rows = min(rows, rng_rows * 64)
+    t0 = time.perf_counter()
+    for f, A, al in data.values():
+        run(f, A, al, (0, rows))
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows * N * K * len(data)
+    return {"value": flops / dt / 1e12, "unit": UNIT, "cores": threads,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"{rows} rows x N={N} x K={K} of each of {len(data)} weight-only GEMMs "
+                      f"({', '.join(data)}), decode + FP32 loop, {dt:.1f} s"}
+
+
+def reference_arm(args):
+    """--impl reference: the reference's own CPU implementation of the path
+    (its host decode primitives + FP32 GEMM loop, oracle/_ref) on the host
+    cores, rank 0 only, one bounded sample of the sweep per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    M = N = K = args.size
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = host_threads()
+    b = O.normal(1, (N, K), 1.0)
+    B16 = O.f32_to_f16_bits(b).reshape(N, K)
+    fmts = {"tf32": O.TF32, "bf16": O.BF16, "e4m3": O.E4M3, "e2m1": O.E2M1}
+    rows = max(threads, 2 * threads)
+    data = []
+    for name, f in fmts.items():
+        a = O.normal(2, (rows, K), 0.02)
+        s = O.per_tensor_scale(a, f)
+        data.append((f, O.quantize(f, a, s), float(np.float32(1) / np.float32(s))))
+    use_ref = O.ref_lib() is not None
+
+    def step():
+        for f, A, al in data:
+            if use_ref:
+                O.ref_cpu_gemm(f, A, B16, rows, N, K, alpha=al, threads=threads)
+            else:
+                O.gemm(f, A, O.F16, B16, rows, N, K, alpha=al, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows * N * K * len(data) * args.steps
+    value = flops / dt / 1e12
+    sample = (f"{rows} rows x N={N} x K={K} per weight-only GEMM, formats {list(fmts)}, reference host decode "
+              f"primitives + FP32 loop per step")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (decoded f16 operands)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"format sweep {M}x{N}x{K} (bounded row sample on the host)", "M": M, "N": N,
+                       "K": K},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
+                             "kind": "reference" if use_ref else "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def traffic_from_profiles(label: str):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic_per_launch.txt")
+    try:
+        for ln in open(path):
+            k, _, v = ln.partition("=")
+            if k.strip() == label:
+                return float(v.strip())
+    except OSError:
+        pass
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--size", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+    tb = load_package()
+    dist = Dist(torch, args.gpus)
+    M = N = K = args.size
+    sw = Sweep(torch, tb, M, N, K, seed=1234 + dist.rank)
+    total_ms, per_op, launches, clock = run_device(torch, tb, sw, args.steps, args.warmup, dist)
+    t_max = dist.max(total_ms)
+    e2e_ms, h2d, d2h = run_e2e(torch, tb, sw, max(2, args.steps // 2), 1)
+    e2e_max = dist.max(e2e_ms)
+    e2e_steps = max(2, args.steps // 2)
+    q = quality(torch, tb, sw)
+    assert tb.device_error() == 0, "a kernel reported a device-side wait timeout"
+
+    step_flops = sw.step_flops()
+    value = dist.world * step_flops * args.steps / (t_max / 1e3) / 1e12
+    peaks = measured_peaks()
+    # per-format and per-kernel figures (rank-local)
+    mean = {k: sum(v) / len(v) for k, v in per_op.items()}
+    formats = {}
+    for name in FORMATS:
+        dec_ms = mean[f"decode_{name}"]
+        formats[name] = {
+            "fused_tflops": sw.flops_per_gemm / mean[f"fused_{name}"] / 1e9,
+            "unfused_tflops": sw.flops_per_gemm / (dec_ms + mean[f"gemm_after_{name}"]) / 1e9,
+            "fused_pct_f16_dense_peak": 100 * sw.flops_per_gemm / mean[f"fused_{name}"] / 1e9 / 2250.0,
+            "decode_gbs": sw.decode_bytes(name) / dec_ms / 1e6,
+            "decode_pct_hbm": 100 * sw.decode_bytes(name) / dec_ms / 1e6 / peaks["hbm_gbs"],
+            **q[name],
+        }
+    formats["native_e4m3"] = {"tflops": sw.flops_per_gemm / mean["native_e4m3"] / 1e9,
+                              "pct_fp8_dense_peak": 100 * sw.flops_per_gemm / mean["native_e4m3"] / 1e9 / 4500.0,
+                              **q["native_e4m3"]}
+    # dominant kernel: the kernel (instantiation) with the largest total time;
+    # the four post-decode GEMMs are one kernel, the tcgen05 FP16 GEMM
+    groups = {}
+    for k, v in per_op.items():
+        groups.setdefault("gemm_f16" if k.startswith("gemm_after_") else k, []).extend(v)
+    totals = {k: sum(v) for k, v in groups.items()}
+    dom = max(totals, key=totals.get)
+    dom_ms = sum(groups[dom]) / len(groups[dom])
+    if dom.startswith("decode_"):
+        nm = dom.split("_", 1)[1]
+        achieved = sw.decode_bytes(nm) / dom_ms / 1e6
+        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"]}
+    else:
+        achieved = sw.flops_per_gemm / dom_ms / 1e9
+        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"]}
+    roof["peak_source"] = f"{peaks['source']} (MEASURED_PEAKS.json burst cuBLAS bf16 / copy)"
+    roof["traffic"] = traffic_from_profiles(dom)
+    roof["share_of_step"] = totals[dom] / total_ms
+    roof["launches_per_step"] = len(groups[dom]) // args.steps
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16xf16->f32 (decoded operands); e4m3xe4m3->f32 native",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "config": {"workload": f"format sweep {M}x{N}x{K}: fused + unfused decode+GEMM for TF32/BF16/E4M3/E2M1, "
+                               f"native E4M3xE4M3; FP32 out", "M": M, "N": N, "K": K,
+                   "gemms_per_step": len(sw.ops()) - len(FORMATS), "l2": "flushed between steps (256 MiB write)",
+                   "parallelism": f"replicas x{dist.world}"},
+        "roofline": roof,
+        "e2e": {"value": dist.world * step_flops * e2e_steps / (e2e_max / 1e3) / 1e12, "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clock,
+        "formats": formats,
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline((M, N, K))
+    dist.close()
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

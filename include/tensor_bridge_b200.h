@@ -122,6 +122,22 @@ tb_status tb_decode_tf32_to_half(const uint32_t* A, const uint32_t* B, uint16_t*
 tb_status tb_decode_fp4_to_half(const uint8_t* A, const uint8_t* B, uint16_t* A16, uint16_t* B16,
                                 int M, int N, int K, tb_stream_t stream);
 
+/* ---- quantize (device-side; the reference quantizes on the host) -------- */
+
+/* dst = Q(src[i] * scale) for i < n (scale 1: Q(src[i])), with Q the reference
+ * quantizer of `fmt`: fp32_to_fp8_e4m3 (fp8.h:43-61), fp32_to_fp8_e5m2
+ * (fp8.h:64-81), fp32_to_fp4_e2m1 (fp4.h:46-53; TB_FMT_E2M1 packs the first
+ * value high, TB_FMT_E2M1_HW low), fp32_to_bf16 (bf16.h:37-48), fp32_to_tf32
+ * (tf32.h:37-44), or FP16 round-to-nearest-even.  Replaces the host loops
+ * `qA[i] = QUANT(hA[i] * ascale)` of bench/bench_formats.cu:64-65,131-132.
+ * Bit-exact to the reference except for signaling-NaN inputs to the FP8
+ * quantizers, whose reference result depends on the host's fminf. */
+tb_status tb_quantize(tb_format fmt, const float* src, void* dst, size_t n, float scale, tb_stream_t stream);
+
+/* *out (a device float) = max |src[i]| over the non-NaN values, the maxabs of
+ * the per-tensor scale FORMAT_MAX / maxabs (bench/bench_formats.cu:128-130). */
+tb_status tb_absmax(const float* src, size_t n, float* out, tb_stream_t stream);
+
 /* ---- GEMMs (tcgen05 tensor cores, TMEM accumulators) --------------------- */
 
 /* D = alpha * A * B^T.  A [M x K] FP16, B [N x K] FP16, FP32 accumulation.

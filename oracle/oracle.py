@@ -74,6 +74,9 @@ def stored_count(fmt: int, n: int) -> int:
 
 def decode(fmt: int, src: np.ndarray, n: int) -> np.ndarray:
     src = np.ascontiguousarray(src)
+    need = stored_count(fmt, n) * np.dtype(stored_dtype(fmt)).itemsize
+    if src.nbytes < need:
+        raise ValueError(f"decode of {n} values needs {need} bytes, got {src.nbytes}")
     out = np.empty(n, dtype=np.uint16)
     lib().oracle_decode(fmt, _c(src), _c(out), n)
     return out

@@ -89,6 +89,8 @@ SIGNATURES = {
     "tb_decode_bf16_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "tb_decode_tf32_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "tb_decode_fp4_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
+    "tb_quantize": (_st, [_i, _p, _p, _sz, _f, _p]),
+    "tb_absmax": (_st, [_p, _sz, _p, _p]),
     "tb_gemm_f16": (_st, [_p, _p, _p, _i, _i, _i, _i, _f, _p]),
     "tb_gemm_fused": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "tb_gemm_fused_workspace": (_sz, [_i, _i, _i, _i]),
@@ -165,6 +167,14 @@ def decode(fmt, src, dst, n: int, stream=None):
 
 def decode_transposed(fmt, src, dst, rows: int, cols: int, stream=None):
     call("tb_decode_transposed", int(fmt), _ptr(src), _ptr(dst), rows, cols, _stream(stream))
+
+
+def quantize(fmt, src, dst, n: int, scale: float = 1.0, stream=None):
+    call("tb_quantize", int(fmt), _ptr(src), _ptr(dst), n, scale, _stream(stream))
+
+
+def absmax(src, n: int, out, stream=None):
+    call("tb_absmax", _ptr(src), n, _ptr(out), _stream(stream))
 
 
 def gemm_f16(A, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):

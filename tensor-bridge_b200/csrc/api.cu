@@ -164,6 +164,26 @@ tb_status tb_fp4_repack_hw(const uint8_t* src, uint8_t* dst, size_t n_bytes, tb_
     return from_cuda(tb::fp4_repack_launch(src, dst, n_bytes, stream, sms), "repack launch");
 }
 
+// ---- quantize ----------------------------------------------------------------
+
+tb_status tb_quantize(tb_format fmt, const float* src, void* dst, size_t n, float scale, tb_stream_t stream) {
+    if (!known_format(fmt)) return fail(TB_ERR_INVALID_ARGUMENT, "bad format %d", (int)fmt);
+    if (n == 0) return TB_OK;
+    if (!src || !dst) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    const int sms = tb::device_info(tb::current_device()).sms;
+    return from_cuda(tb::quantize_launch(fmt, src, dst, n, scale, stream, sms), "quantize launch");
+}
+
+tb_status tb_absmax(const float* src, size_t n, float* out, tb_stream_t stream) {
+    if (!out || (n && !src)) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    const int sms = tb::device_info(tb::current_device()).sms;
+    return from_cuda(tb::absmax_launch(src, n, out, stream, sms), "absmax launch");
+}
+
 // ---- GEMMs -------------------------------------------------------------------
 
 tb_status tb_gemm_f16(const uint16_t* A, const uint16_t* B, void* D, int M, int N, int K, tb_out_type out, float alpha,

@@ -92,16 +92,25 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
 // ---------------------------------------------------------------------------------
 // Configurations
 
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemBudget = 216 * 1024;
 
+// Stage counts per configuration.  Fused mode: the decoded-A ring needs two
+// tiles for large N (decode of k-block i+1 overlaps the MMAs of k-block i) and
+// four for narrow N (short MMAs); the operand ring takes B tiles; the raw-A
+// ring gets the rest (up to 12 stages of prefetch, at least 2).
 template <int BN, int MODE, int FMT>
 struct Pick {
-    static constexpr int SD = MODE == kModeDecode ? (BN >= 128 ? 2 : 4) : 0;
-    static constexpr int RA = MODE == kModeDecode ? 128 * raw_row_bytes(FMT) : 128 * 128;
-    static constexpr int STAGE = RA + BN * 128;
-    static constexpr int SR0 = (kSmemBudget - SD * 128 * 128) / STAGE;
-    static constexpr int SR = SR0 > 12 ? 12 : (SR0 < 2 ? 2 : SR0);
-    using Cfg = GemmCfg<BN, MODE, FMT, SR, SD>;
+    static constexpr bool kDec = MODE == kModeDecode;
+    static constexpr int A = 128 * 128, B = BN * 128;
+    static constexpr int SD = kDec ? (BN >= 128 ? 2 : 4) : 0;
+    static constexpr int RA = kDec ? 128 * raw_row_bytes(FMT) : 0;
+    static constexpr int S_DEC0 = (kSmemBudget - SD * A - 3 * RA) / B;
+    static constexpr int S_DEC = S_DEC0 > 6 ? 6 : (S_DEC0 < 2 ? 2 : S_DEC0);
+    static constexpr int S_PLAIN0 = kSmemBudget / (A + B);
+    static constexpr int S = kDec ? S_DEC : (S_PLAIN0 > 12 ? 12 : S_PLAIN0);
+    static constexpr int SA0 = kDec ? (kSmemBudget - SD * A - S * B) / RA : 0;
+    static constexpr int SA = kDec ? (SA0 > 12 ? 12 : (SA0 < 2 ? 2 : SA0)) : 0;
+    using Cfg = GemmCfg<BN, MODE, FMT, S, SA, SD>;
 };
 
 template <class C>

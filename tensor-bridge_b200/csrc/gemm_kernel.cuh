@@ -4,17 +4,22 @@
 //
 // One CTA per SM walks a static list of work units (128 x BN output tiles,
 // optionally split along K).  Roles:
-//   warp 0      TMA producer: raw A (or FP16 / FP8 A) and B tiles into an
-//               R-stage ring of shared memory (one elected lane)
-//   warp 1      TMEM allocator and MMA issuer: one lane issues
-//               tcgen05.mma (M = 128, N = BN, 32 bytes of K per instruction)
-//               into one of two TMEM accumulators
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp owns the
-//               32 TMEM lanes = tile rows of its warp-id quarter), scale by
-//               alpha, convert, store to global memory
-//   warps 6..   (fused mode only) decode warps: read the raw A tile that TMA
-//               staged, decode it to FP16 and write it, 128-byte swizzled,
-//               into a D-stage ring the MMA reads directly
+//   warp 0      TMA producer of B (and, when A needs no decode, of A) into
+//               the operand ring (one elected lane)
+//   warp 1      TMEM allocator and MMA issuer: one lane issues tcgen05.mma
+//               (M = 128, N = BN, 32 bytes of K per instruction) into one of
+//               two TMEM accumulators, so the epilogue of tile t overlaps the
+//               main loop of tile t+1
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp owns the 32
+//               TMEM lanes = tile rows of its warp-id quarter), scale by alpha,
+//               convert, store to global memory
+//   fused mode only:
+//   warp 6      TMA producer of the raw (stored-format) A tiles into their own
+//               ring, which the decode warps free as soon as they have read a
+//               tile -- raw A is prefetched independently of the MMA
+//   warps 7..   decode warps: read a staged raw A tile, decode it to FP16 and
+//               write it, 128-byte swizzled, into the decoded-A ring the MMA
+//               reads directly; decoded weights never leave shared memory
 //
 // Shared-memory operand tiles use the canonical K-major SWIZZLE_128B layout:
 // 128-byte rows (64 FP16 or 128 FP8 values of K), 8-row groups of 1024 bytes,
@@ -22,8 +27,9 @@
 // writes that layout itself; the decode warps write it explicitly.
 //
 // Every mbarrier wait is bounded (tb_ptx.cuh): on expiry the kernel sets the
-// device error word, all roles leave their loops, and the TMEM allocation is
-// released before the CTA exits.
+// device error word, all roles leave their loops, asynchronous copies and
+// MMAs already issued are drained, and the TMEM allocation is released before
+// the CTA exits.
 #pragma once
 
 #include <cstdint>
@@ -44,48 +50,61 @@ __host__ __device__ constexpr int raw_row_bytes(int fmt) {
     return fmt == kE2M1 ? 32 : fmt == kBF16 ? 128 : fmt == kTF32 ? 256 : fmt == kF16 ? 128 : 64;
 }
 
-__host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 __host__ __device__ constexpr int pow2_at_least(int x) {
     return x <= 32 ? 32 : x <= 64 ? 64 : x <= 128 ? 128 : x <= 256 ? 256 : 512;
 }
 
 // Compile-time configuration of one kernel instance.
-template <int BN_, int MODE_, int FMT_, int SR_, int SD_>
+//   S_  operand-ring stages: B tiles (plus A tiles when A needs no decode)
+//   SA_ raw-A ring stages (fused mode)
+//   SD_ decoded-A ring stages (fused mode)
+template <int BN_, int MODE_, int FMT_, int S_, int SA_, int SD_>
 struct GemmCfg {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
     static constexpr int MODE = MODE_;
     static constexpr int FMT = FMT_;
-    static constexpr int SR = SR_;                          // R ring stages (A-or-raw + B)
-    static constexpr int SD = MODE == kModeDecode ? SD_ : 0;  // D ring stages (decoded A)
-    static constexpr int ND = MODE == kModeDecode ? 4 : 0;    // decode warps
-    static constexpr int NUM_THREADS = 192 + ND * 32;
+    static constexpr bool kDecode = MODE == kModeDecode;
+    static constexpr int S = S_;
+    static constexpr int SA = kDecode ? SA_ : 0;
+    static constexpr int SD = kDecode ? SD_ : 0;
+    static constexpr int ND = kDecode ? 8 : 0;  // decode warps
+    static constexpr int DECODE_WARP0 = 7;
+    static constexpr int NUM_THREADS = kDecode ? (DECODE_WARP0 + ND) * 32 : 192;
     static constexpr int DECODE_THREADS = ND * 32;
 
-    static constexpr int A_BYTES = BM * 128;  // one swizzled 128 x 128-byte operand tile
+    static constexpr int A_BYTES = BM * 128;  // one swizzled 128-row x 128-byte operand tile
     static constexpr int B_BYTES = BN * 128;
-    static constexpr int RA_BYTES = MODE == kModeDecode ? BM * raw_row_bytes(FMT) : A_BYTES;
-    // K elements per k-block and the TMA inner-coordinate step of A and B.
+    static constexpr int RA_BYTES = kDecode ? BM * raw_row_bytes(FMT) : 0;
+    // K elements per k-block and the TMA inner-coordinate steps.
     static constexpr int KB_ELEMS = MODE == kModeNative8 ? 128 : 64;
-    static constexpr int A_X_STEP = MODE == kModeDecode && FMT == kE2M1 ? 32 : KB_ELEMS;
+    static constexpr int A_X_STEP = kDecode && FMT == kE2M1 ? 32 : KB_ELEMS;
     static constexpr int B_X_STEP = KB_ELEMS;
 
-    static constexpr int OFF_B = 0;
-    static constexpr int OFF_RA = OFF_B + SR * B_BYTES;
-    static constexpr int OFF_D = OFF_RA + SR * RA_BYTES;
+    // Shared-memory layout (offsets from a 1024-byte aligned base).
+    static constexpr int OFF_B = 0;                              // S x B tile
+    static constexpr int OFF_A = OFF_B + S * B_BYTES;            // S x A tile (non-fused modes)
+    static constexpr int OFF_RA = OFF_A + (kDecode ? 0 : S * A_BYTES);  // SA x raw A tile
+    static constexpr int OFF_D = OFF_RA + SA * RA_BYTES;         // SD x decoded A tile
     static constexpr int OFF_BAR = OFF_D + SD * A_BYTES;
-    static constexpr int NUM_BARS = 2 * SR + 2 * SD + 5;
+    static constexpr int NUM_BARS = 2 * S + 2 * SA + 2 * SD + 5;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to 1024-align the base
 
     static constexpr int TMEM_COLS = pow2_at_least(2 * BN);
     static constexpr int CW = BN < 32 ? BN : 32;  // epilogue column chunk
 
-    // MMA formats: kind::f16 with FP16 operands, or kind::f8f6f4 with E4M3.
+    // MMA: kind::f16 with FP16 operands, or kind::f8f6f4 with E4M3 (same
+    // format code 0), FP32 accumulation, K-major operands.
     static constexpr uint32_t IDESC = idesc_make(0u, 0u, BM, BN);
+
+    // Raw A units (16 bytes) per k-block and per decode thread.
+    static constexpr int UNITS = kDecode ? RA_BYTES / 16 : 0;
+    static constexpr int UPT = kDecode ? UNITS / (DECODE_THREADS > 0 ? DECODE_THREADS : 1) : 0;
 
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "BN");
     static_assert(B_BYTES % 1024 == 0 && RA_BYTES % 1024 == 0, "stage alignment");
+    static_assert(!kDecode || (UNITS % (DECODE_THREADS > 0 ? DECODE_THREADS : 1) == 0 && UPT >= 1), "decode split");
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
@@ -102,21 +121,56 @@ struct GemmArgs {
     float* ws;       // split-K partials [splits][M][N] (FP32), when splits > 1
 };
 
+// ---- explicit shared-memory accesses (32-bit shared addresses) ----------------------
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ void sts64(uint32_t a, uint32_t x, uint32_t y) {
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+
 // Byte offset of 16-byte chunk `chunk` of row `row` in a swizzled tile.
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
     return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// Decode raw 16-byte unit q of a staged A tile into the swizzled FP16 tile.
+// True (warp-uniformly) if any lane's unit holds a code that the fast decode
+// path does not reproduce; those units take the scalar reference path.
 template <int FMT>
-__device__ __forceinline__ void decode_unit(const uint8_t* raw, uint8_t* dst, int q) {
-    const uint4 in = *reinterpret_cast<const uint4*>(raw + q * 16);
+__device__ __forceinline__ bool unit_needs_scalar(const uint4& in) {
+    if constexpr (FMT == kE4M3) {
+        const uint32_t m = e4m3_special_mask(in.x) | e4m3_special_mask(in.y) | e4m3_special_mask(in.z) |
+                           e4m3_special_mask(in.w);
+        return __any_sync(0xFFFFFFFFu, m != 0u);
+    } else if constexpr (FMT == kBF16) {
+        const uint32_t m = bf16_nan_lanes(in.x) | bf16_nan_lanes(in.y) | bf16_nan_lanes(in.z) | bf16_nan_lanes(in.w);
+        return __any_sync(0xFFFFFFFFu, m != 0u);
+    } else {
+        return false;
+    }
+}
+
+// Decode raw 16-byte unit q (already loaded into `in`) of a staged A tile and
+// store it into the swizzled FP16 tile at shared address `dst`.
+template <int FMT>
+__device__ __forceinline__ void decode_store_unit(const uint4& in, uint32_t dst, int q) {
     if constexpr (FMT == kE4M3 || FMT == kE5M2 || FMT == kE2M1U) {
         const int row = q >> 2, c0 = (q & 3) * 2;
         uint32_t o[8];
         if constexpr (FMT == kE4M3) {
-            decode_e4m3_x4(in.x, o[0], o[1]); decode_e4m3_x4(in.y, o[2], o[3]);
-            decode_e4m3_x4(in.z, o[4], o[5]); decode_e4m3_x4(in.w, o[6], o[7]);
+            if (unit_needs_scalar<kE4M3>(in)) {
+                decode_e4m3_x4_scalar(in.x, o[0], o[1]); decode_e4m3_x4_scalar(in.y, o[2], o[3]);
+                decode_e4m3_x4_scalar(in.z, o[4], o[5]); decode_e4m3_x4_scalar(in.w, o[6], o[7]);
+            } else {
+                decode_e4m3_x4_fast(in.x, o[0], o[1]); decode_e4m3_x4_fast(in.y, o[2], o[3]);
+                decode_e4m3_x4_fast(in.z, o[4], o[5]); decode_e4m3_x4_fast(in.w, o[6], o[7]);
+            }
         } else if constexpr (FMT == kE5M2) {
             decode_e5m2_x4(in.x, o[0], o[1]); decode_e5m2_x4(in.y, o[2], o[3]);
             decode_e5m2_x4(in.z, o[4], o[5]); decode_e5m2_x4(in.w, o[6], o[7]);
@@ -124,27 +178,31 @@ __device__ __forceinline__ void decode_unit(const uint8_t* raw, uint8_t* dst, in
             decode_e2m1_unpacked_x4(in.x, o[0], o[1]); decode_e2m1_unpacked_x4(in.y, o[2], o[3]);
             decode_e2m1_unpacked_x4(in.z, o[4], o[5]); decode_e2m1_unpacked_x4(in.w, o[6], o[7]);
         }
-        *reinterpret_cast<uint4*>(dst + swz(row, c0)) = make_uint4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<uint4*>(dst + swz(row, c0 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+        sts128(dst + swz(row, c0), o[0], o[1], o[2], o[3]);
+        sts128(dst + swz(row, c0 + 1), o[4], o[5], o[6], o[7]);
     } else if constexpr (FMT == kE2M1) {
         const int row = q >> 1, c0 = (q & 1) * 4;
         uint32_t o[4];
         decode_e2m1_packed_x8(in.x, o);
-        *reinterpret_cast<uint4*>(dst + swz(row, c0 + 0)) = make_uint4(o[0], o[1], o[2], o[3]);
+        sts128(dst + swz(row, c0 + 0), o[0], o[1], o[2], o[3]);
         decode_e2m1_packed_x8(in.y, o);
-        *reinterpret_cast<uint4*>(dst + swz(row, c0 + 1)) = make_uint4(o[0], o[1], o[2], o[3]);
+        sts128(dst + swz(row, c0 + 1), o[0], o[1], o[2], o[3]);
         decode_e2m1_packed_x8(in.z, o);
-        *reinterpret_cast<uint4*>(dst + swz(row, c0 + 2)) = make_uint4(o[0], o[1], o[2], o[3]);
+        sts128(dst + swz(row, c0 + 2), o[0], o[1], o[2], o[3]);
         decode_e2m1_packed_x8(in.w, o);
-        *reinterpret_cast<uint4*>(dst + swz(row, c0 + 3)) = make_uint4(o[0], o[1], o[2], o[3]);
+        sts128(dst + swz(row, c0 + 3), o[0], o[1], o[2], o[3]);
     } else if constexpr (FMT == kBF16) {
         const int row = q >> 3, c = q & 7;
-        *reinterpret_cast<uint4*>(dst + swz(row, c)) =
-            make_uint4(decode_bf16_x2(in.x), decode_bf16_x2(in.y), decode_bf16_x2(in.z), decode_bf16_x2(in.w));
+        if (unit_needs_scalar<kBF16>(in)) {
+            sts128(dst + swz(row, c), decode_bf16_x2_scalar(in.x), decode_bf16_x2_scalar(in.y),
+                   decode_bf16_x2_scalar(in.z), decode_bf16_x2_scalar(in.w));
+        } else {
+            sts128(dst + swz(row, c), decode_bf16_x2_fast(in.x), decode_bf16_x2_fast(in.y),
+                   decode_bf16_x2_fast(in.z), decode_bf16_x2_fast(in.w));
+        }
     } else if constexpr (FMT == kTF32) {
         const int row = q >> 4, c = (q & 15) >> 1;
-        *reinterpret_cast<uint2*>(dst + swz(row, c) + (q & 1) * 8) =
-            make_uint2(decode_tf32_x2(in.x, in.y), decode_tf32_x2(in.z, in.w));
+        sts64(dst + swz(row, c) + (q & 1) * 8, decode_tf32_x2(in.x, in.y), decode_tf32_x2(in.z, in.w));
     }
 }
 
@@ -155,6 +213,11 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& p, int u, int& tm, i
     const int r = u / p.tiles_m;
     tn = r % p.tiles_n;
     sp = r / p.tiles_n;
+}
+
+__device__ __forceinline__ void unit_kblocks(const GemmArgs& p, int sp, int& kb0, int& kb1) {
+    kb0 = sp * p.kb_per_split;
+    kb1 = min(p.num_kb, kb0 + p.kb_per_split);
 }
 
 template <int CW>
@@ -218,6 +281,15 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int sp, int r
     }
 }
 
+// Abort path of a TMA producer: let the copies already issued into a ring of
+// `stages` stages land before the CTA's shared memory goes away.
+__device__ __forceinline__ void drain_ring(uint64_t* full, int stages, long long issued) {
+    for (int st = 0; st < stages && st < issued; ++st) {
+        const long long last = st + static_cast<long long>(stages) * ((issued - 1 - st) / stages);
+        mbar_wait_drain(&full[st], static_cast<uint32_t>((last / stages) & 1));
+    }
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs p) {
@@ -227,13 +299,15 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     const uint32_t sbase = smem_addr(smem);
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* r_full = bars;
-    uint64_t* r_empty = bars + C::SR;
-    uint64_t* d_full = bars + 2 * C::SR;
-    uint64_t* d_empty = d_full + C::SD;
-    uint64_t* acc_full = d_empty + C::SD;
-    uint64_t* acc_empty = acc_full + 2;
-    uint64_t* fin_bar = acc_empty + 2;  // MMA drain on the abort path
+    uint64_t* b_full = bars;                  // operand ring: TMA tx complete
+    uint64_t* b_empty = b_full + C::S;        // operand ring: MMA done reading
+    uint64_t* a_full = b_empty + C::S;        // raw-A ring: TMA tx complete
+    uint64_t* a_empty = a_full + C::SA;       // raw-A ring: decode warps done reading
+    uint64_t* d_full = a_empty + C::SA;       // decoded-A ring: decode warps done writing
+    uint64_t* d_empty = d_full + C::SD;       // decoded-A ring: MMA done reading
+    uint64_t* acc_full = d_empty + C::SD;     // accumulator ready for the epilogue
+    uint64_t* acc_empty = acc_full + 2;       // accumulator drained by the epilogue
+    uint64_t* fin_bar = acc_empty + 2;        // MMA drain on the abort path
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(fin_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -241,12 +315,16 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::SR; ++s) {
-            mbar_init(&r_full[s], 1);
-            mbar_init(&r_empty[s], C::MODE == kModeDecode ? 1 + C::DECODE_THREADS : 1);
+        for (int s = 0; s < C::S; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (int s = 0; s < C::SA; ++s) {
+            mbar_init(&a_full[s], 1);
+            mbar_init(&a_empty[s], C::ND);
         }
         for (int s = 0; s < C::SD; ++s) {
-            mbar_init(&d_full[s], C::DECODE_THREADS);
+            mbar_init(&d_full[s], C::ND);
             mbar_init(&d_empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -271,63 +349,56 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer: B (and A when no decode) ----------------
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
             long long issued = 0;
             bool ok = true;
+            constexpr uint32_t kTx = C::B_BYTES + (C::kDecode ? 0 : C::A_BYTES);
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-                int tm, tn, sp;
+                int tm, tn, sp, kb0, kb1;
                 unit_coords(p, u, tm, tn, sp);
-                const int kb0 = sp * p.kb_per_split;
-                const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+                unit_kblocks(p, sp, kb0, kb1);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(&r_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&r_full[s], C::RA_BYTES + C::B_BYTES);
-                    tma_load_2d(smem + C::OFF_RA + s * C::RA_BYTES, &tmA, &r_full[s], kb * C::A_X_STEP, tm * C::BM);
-                    tma_load_2d(smem + C::OFF_B + s * C::B_BYTES, &tmB, &r_full[s], kb * C::B_X_STEP, tn * C::BN);
+                    if (!mbar_wait(&b_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&b_full[s], kTx);
+                    if constexpr (!C::kDecode)
+                        tma_load_2d(smem + C::OFF_A + s * C::A_BYTES, &tmA, &b_full[s], kb * C::KB_ELEMS, tm * C::BM);
+                    tma_load_2d(smem + C::OFF_B + s * C::B_BYTES, &tmB, &b_full[s], kb * C::B_X_STEP, tn * C::BN);
                     ++issued;
-                    if (++s == C::SR) { s = 0; ph ^= 1u; }
+                    if (++s == C::S) { s = 0; ph ^= 1u; }
                 }
             }
-            if (!ok) {
-                // Abort path: let the copies already issued land before the
-                // CTA's shared memory goes away.
-                for (int st = 0; st < C::SR && st < issued; ++st) {
-                    const long long last = st + (long long)C::SR * ((issued - 1 - st) / C::SR);
-                    mbar_wait_drain(&r_full[st], static_cast<uint32_t>((last / C::SR) & 1));
-                }
-            }
+            if (!ok) drain_ring(b_full, C::S, issued);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            int rs = 0, ds = 0;
-            uint32_t rph = 0, dph = 0;
+            int bs = 0, ds = 0;
+            uint32_t bph = 0, dph = 0;
             int t = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x, ++t) {
-                int tm, tn, sp;
+                int tm, tn, sp, kb0, kb1;
                 unit_coords(p, u, tm, tn, sp);
-                const int kb0 = sp * p.kb_per_split;
-                const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+                unit_kblocks(p, sp, kb0, kb1);
                 const int acc = t & 1;
                 const uint32_t aph = (t >> 1) & 1;
                 if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::BN);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(&r_full[rs], rph, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait(&b_full[bs], bph, abort_flag)) { ok = false; break; }
                     uint32_t a_off;
-                    if constexpr (C::MODE == kModeDecode) {
+                    if constexpr (C::kDecode) {
                         if (!mbar_wait(&d_full[ds], dph, abort_flag)) { ok = false; break; }
                         a_off = C::OFF_D + ds * C::A_BYTES;
                     } else {
-                        a_off = C::OFF_RA + rs * C::RA_BYTES;
+                        a_off = C::OFF_A + bs * C::A_BYTES;
                     }
                     tc_fence_after();
-                    const uint32_t b_off = C::OFF_B + rs * C::B_BYTES;
+                    const uint32_t b_off = C::OFF_B + bs * C::B_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t ad = sdesc_k_sw128(sbase + a_off + kk * 32);
@@ -336,12 +407,12 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                         if constexpr (C::MODE == kModeNative8) mma_f8f6f4_ss(d_tmem, ad, bd, C::IDESC, accum);
                         else mma_f16_ss(d_tmem, ad, bd, C::IDESC, accum);
                     }
-                    if constexpr (C::MODE == kModeDecode) {
+                    if constexpr (C::kDecode) {
                         mma_commit(&d_empty[ds]);
                         if (++ds == C::SD) { ds = 0; dph ^= 1u; }
                     }
-                    mma_commit(&r_empty[rs]);
-                    if (++rs == C::SR) { rs = 0; rph ^= 1u; }
+                    mma_commit(&b_empty[bs]);
+                    if (++bs == C::S) { bs = 0; bph ^= 1u; }
                 }
                 if (!ok) break;
                 mma_commit(&acc_full[acc]);
@@ -377,30 +448,56 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
         }
-    } else {
-        // ---------------- decode warps (fused mode) ----------------
-        if constexpr (C::MODE == kModeDecode) {
-            constexpr int UNITS = C::RA_BYTES / 16;
-            const int dt = threadIdx.x - 192;
-            int rs = 0, ds = 0;
-            uint32_t rph = 0, dph = 0;
+    } else if constexpr (C::kDecode) {
+        if (warp == 6) {
+            // ---------------- TMA producer: raw A ----------------
+            if (lane == 0) {
+                int s = 0;
+                uint32_t ph = 0;
+                long long issued = 0;
+                bool ok = true;
+                for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+                    int tm, tn, sp, kb0, kb1;
+                    unit_coords(p, u, tm, tn, sp);
+                    unit_kblocks(p, sp, kb0, kb1);
+                    for (int kb = kb0; kb < kb1; ++kb) {
+                        if (!mbar_wait(&a_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&a_full[s], C::RA_BYTES);
+                        tma_load_2d(smem + C::OFF_RA + s * C::RA_BYTES, &tmA, &a_full[s], kb * C::A_X_STEP, tm * C::BM);
+                        ++issued;
+                        if (++s == C::SA) { s = 0; ph ^= 1u; }
+                    }
+                }
+                if (!ok) drain_ring(a_full, C::SA, issued);
+            }
+        } else {
+            // ---------------- decode warps ----------------
+            const int dt = threadIdx.x - C::DECODE_WARP0 * 32;
+            int as = 0, ds = 0;
+            uint32_t aph = 0, dph = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-                int tm, tn, sp;
+                int tm, tn, sp, kb0, kb1;
                 unit_coords(p, u, tm, tn, sp);
-                const int kb0 = sp * p.kb_per_split;
-                const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+                unit_kblocks(p, sp, kb0, kb1);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(&r_full[rs], rph, abort_flag)) { ok = false; break; }
-                    if (!mbar_wait(&d_empty[ds], dph ^ 1u, abort_flag)) { ok = false; break; }
-                    const uint8_t* raw = smem + C::OFF_RA + rs * C::RA_BYTES;
-                    uint8_t* dst = smem + C::OFF_D + ds * C::A_BYTES;
-#pragma unroll 4
-                    for (int q = dt; q < UNITS; q += C::DECODE_THREADS) decode_unit<C::FMT>(raw, dst, q);
+                    bool w_ok = mbar_wait(&a_full[as], aph, abort_flag);
+                    w_ok = w_ok && mbar_wait(&d_empty[ds], dph ^ 1u, abort_flag);
+                    if (!__all_sync(0xFFFFFFFFu, w_ok)) { ok = false; break; }
+                    const uint32_t raw = sbase + C::OFF_RA + as * C::RA_BYTES;
+                    const uint32_t dst = sbase + C::OFF_D + ds * C::A_BYTES;
+                    uint4 in[C::UPT];
+#pragma unroll
+                    for (int j = 0; j < C::UPT; ++j) in[j] = lds128(raw + (dt + j * C::DECODE_THREADS) * 16);
+                    // Raw tile fully read by this warp: release it to the raw-A producer.
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_empty[as]);
+#pragma unroll
+                    for (int j = 0; j < C::UPT; ++j) decode_store_unit<C::FMT>(in[j], dst, dt + j * C::DECODE_THREADS);
                     fence_proxy_async_smem();
-                    mbar_arrive(&d_full[ds]);
-                    mbar_arrive(&r_empty[rs]);
-                    if (++rs == C::SR) { rs = 0; rph ^= 1u; }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&d_full[ds]);
+                    if (++as == C::SA) { as = 0; aph ^= 1u; }
                     if (++ds == C::SD) { ds = 0; dph ^= 1u; }
                 }
             }

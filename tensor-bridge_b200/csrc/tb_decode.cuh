@@ -51,16 +51,23 @@ __device__ __forceinline__ uint32_t e4m3_special_mask(uint32_t w) {
     return (is_nan | (man_nz & ~exp_nz)) & 0x80808080u;
 }
 
-// Four E4M3 codes (byte 0 first) -> four FP16 values in o[0..1].
+// Four E4M3 codes (byte 0 first) -> four FP16 values in o0, o1.  Fast path:
+// valid when e4m3_special_mask(w) == 0.
+__device__ __forceinline__ void decode_e4m3_x4_fast(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    o0 = cvt_e4m3x2(static_cast<uint16_t>(w & 0xFFFFu));
+    o1 = cvt_e4m3x2(static_cast<uint16_t>(w >> 16));
+}
+
+// Scalar path: the reference rule code by code (valid for every code).
+__device__ __forceinline__ void decode_e4m3_x4_scalar(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    using tensor_bridge::e4m3_to_half_bits;
+    o0 = pack2(e4m3_to_half_bits(w & 0xFFu), e4m3_to_half_bits((w >> 8) & 0xFFu));
+    o1 = pack2(e4m3_to_half_bits((w >> 16) & 0xFFu), e4m3_to_half_bits(w >> 24));
+}
+
 __device__ __forceinline__ void decode_e4m3_x4(uint32_t w, uint32_t& o0, uint32_t& o1) {
-    if (e4m3_special_mask(w) == 0u) {
-        o0 = cvt_e4m3x2(static_cast<uint16_t>(w & 0xFFFFu));
-        o1 = cvt_e4m3x2(static_cast<uint16_t>(w >> 16));
-    } else {
-        using tensor_bridge::e4m3_to_half_bits;
-        o0 = pack2(e4m3_to_half_bits(w & 0xFFu), e4m3_to_half_bits((w >> 8) & 0xFFu));
-        o1 = pack2(e4m3_to_half_bits((w >> 16) & 0xFFu), e4m3_to_half_bits(w >> 24));
-    }
+    if (e4m3_special_mask(w) == 0u) decode_e4m3_x4_fast(w, o0, o1);
+    else decode_e4m3_x4_scalar(w, o0, o1);
 }
 
 // ---- E5M2: each code is the top byte of its FP16 value -------------------------------
@@ -127,17 +134,26 @@ __device__ __forceinline__ uint32_t lane_mask_bit15(uint32_t x) { return prmt(x,
 // subnormal results to a signed zero (the reference maps every BF16 value
 // below 2^-14 to zero; no BF16 value below 2^-14 rounds up to 2^-14).  BF16
 // NaN lanes take the scalar path (the reference encodes them as 0x7E00).
-__device__ __forceinline__ uint32_t decode_bf16_x2(uint32_t w) {
-    const uint32_t nan_lanes = ((w & 0x7FFF7FFFu) + 0x007F007Fu) & 0x80008000u;
-    if (nan_lanes != 0u) {
-        return pack2(tensor_bridge::bf16_to_half_bits(w & 0xFFFFu), tensor_bridge::bf16_to_half_bits(w >> 16));
-    }
+__device__ __forceinline__ uint32_t bf16_nan_lanes(uint32_t w) {
+    return ((w & 0x7FFF7FFFu) + 0x007F007Fu) & 0x80008000u;
+}
+
+__device__ __forceinline__ uint32_t decode_bf16_x2_scalar(uint32_t w) {
+    return pack2(tensor_bridge::bf16_to_half_bits(w & 0xFFFFu), tensor_bridge::bf16_to_half_bits(w >> 16));
+}
+
+// Fast path, valid when bf16_nan_lanes(w) == 0.
+__device__ __forceinline__ uint32_t decode_bf16_x2_fast(uint32_t w) {
     const float lo = __uint_as_float(w << 16);
     const float hi = __uint_as_float(w & 0xFFFF0000u);
     uint32_t h;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
     const uint32_t normal = lane_mask_bit15((h & 0x7C007C00u) + 0x7C007C00u);
     return h & (normal | 0x80008000u);
+}
+
+__device__ __forceinline__ uint32_t decode_bf16_x2(uint32_t w) {
+    return bf16_nan_lanes(w) != 0u ? decode_bf16_x2_scalar(w) : decode_bf16_x2_fast(w);
 }
 
 // ---- TF32 ---------------------------------------------------------------------------

@@ -14,6 +14,10 @@ cudaError_t decode_transposed_launch(int fmt, const void* src, uint16_t* dst, in
 cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms);
 size_t stored_bytes(int fmt, size_t n);
 
+// quantize.cu
+cudaError_t quantize_launch(int fmt, const float* src, void* dst, size_t n, float scale, cudaStream_t st, int sms);
+cudaError_t absmax_launch(const float* src, size_t n, float* out, cudaStream_t st, int sms);
+
 // gemm.cu
 enum class GemmKind { kF16, kFused, kNative };
 
