@@ -92,25 +92,29 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
 // ---------------------------------------------------------------------------------
 // Configurations
 
-constexpr int kSmemBudget = 216 * 1024;
+constexpr int kSmemBudget = 224 * 1024;
 
-// Stage counts per configuration.  Fused mode: the decoded-A ring needs two
-// tiles for large N (decode of k-block i+1 overlaps the MMAs of k-block i) and
-// four for narrow N (short MMAs); the operand ring takes B tiles; the raw-A
-// ring gets the rest (up to 12 stages of prefetch, at least 2).
+// Stage counts per configuration.  An operand-ring stage holds a B tile and
+// an A tile; fused mode adds a raw-A ring (whose stages also carry the B tiles
+// for narrow tiles, BN <= 64).  Fused: up to four operand stages and the rest
+// (at least two, at most eight) raw stages.  The decode round DK is the raw
+// stage's k-blocks, capped at two for wide tiles and four for narrow ones
+// (and below S).
 template <int BN, int MODE, int FMT>
 struct Pick {
     static constexpr bool kDec = MODE == kModeDecode;
     static constexpr int A = 128 * 128, B = BN * 128;
-    static constexpr int SD = kDec ? (BN >= 128 ? 2 : 4) : 0;
-    static constexpr int RA = kDec ? 128 * raw_row_bytes(FMT) : 0;
-    static constexpr int S_DEC0 = (kSmemBudget - SD * A - 3 * RA) / B;
-    static constexpr int S_DEC = S_DEC0 > 6 ? 6 : (S_DEC0 < 2 ? 2 : S_DEC0);
-    static constexpr int S_PLAIN0 = kSmemBudget / (A + B);
-    static constexpr int S = kDec ? S_DEC : (S_PLAIN0 > 12 ? 12 : S_PLAIN0);
-    static constexpr int SA0 = kDec ? (kSmemBudget - SD * A - S * B) / RA : 0;
-    static constexpr int SA = kDec ? (SA0 > 12 ? 12 : (SA0 < 2 ? 2 : SA0)) : 0;
-    using Cfg = GemmCfg<BN, MODE, FMT, S, SA, SD>;
+    static constexpr int RK = kDec ? raw_kblocks(FMT) : 1;
+    static constexpr int RA = kDec ? raw_stage_bytes(FMT) + (BN <= 64 ? RK * B : 0) : 0;
+    static constexpr int S_MAX = kDec ? (BN >= 128 ? 4 : 8) : 12;
+    static constexpr int S0 = (kSmemBudget - 2 * RA) / (A + B);
+    static constexpr int S = S0 > S_MAX ? S_MAX : (S0 < 2 ? 2 : S0);
+    static constexpr int SA0 = kDec ? (kSmemBudget - S * (A + B)) / RA : 0;
+    static constexpr int SA = kDec ? (SA0 > 8 ? 8 : SA0) : 0;
+    static constexpr int DK0 = RK < (BN >= 128 ? 2 : 4) ? RK : (BN >= 128 ? 2 : 4);
+    // power of two dividing RK, at most S - 1
+    static constexpr int DK = DK0 <= S - 1 ? DK0 : (DK0 / 2 <= S - 1 ? DK0 / 2 : 1);
+    using Cfg = GemmCfg<BN, MODE, FMT, S, SA, DK>;
 };
 
 template <class C>
@@ -171,15 +175,18 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
         ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
         ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.B, K, r.N, K, 128, BN, CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
+        // Raw A: 128-byte boxes, 128-byte swizzle (the decode warps read the
+        // swizzled layout).
+        constexpr uint32_t bx = raw_box_elems(FMT);
         if constexpr (FMT == kE2M1) {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K / 2, r.M, K / 2, 32, 128,
-                          CU_TENSOR_MAP_SWIZZLE_NONE);
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K / 2, r.M, K / 2, bx, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
         } else if constexpr (FMT == kBF16) {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
         } else if constexpr (FMT == kTF32) {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT32, r.A, K, r.M, K * 4, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT32, r.A, K, r.M, K * 4, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
         } else {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
         }
         ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, BN,
                             CU_TENSOR_MAP_SWIZZLE_128B);
@@ -214,7 +221,10 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
         splits = r.force_splits ? r.force_splits : choose_splits(tiles_m * tiles_n, num_kb, sms);
         splits = std::max(1, std::min(splits, num_kb));
     }
+    // Each split starts on a raw-stage boundary of the fused kernel.
+    const int rk = r.kind == GemmKind::kFused ? raw_kblocks(r.a_fmt) : 1;
     int kb_per = (num_kb + splits - 1) / splits;
+    kb_per = (kb_per + rk - 1) / rk * rk;
     splits = (num_kb + kb_per - 1) / kb_per;
     if (splits > 1) {
         const size_t need = static_cast<size_t>(splits) * r.M * r.N * sizeof(float);

@@ -42,13 +42,13 @@ __device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) {
 
 // Bit 7 of each byte set where the E4M3 code needs the scalar path: exponent
 // field 0 with a non-zero mantissa (a subnormal, flushed by the reference) or
-// magnitude 0x7F (NaN, which the reference encodes as 0x7E00).
+// magnitude 0x7F (NaN, which the reference encodes as 0x7E00).  With
+// m = code & 0x7F (no byte carries out of its lane):
+//   m + 0x7F has bit 7 iff m >= 1;  m + 0x78 iff m >= 8;  m + 0x01 iff m == 0x7F.
 __device__ __forceinline__ uint32_t e4m3_special_mask(uint32_t w) {
-    const uint32_t mag = w & 0x7F7F7F7Fu;
-    const uint32_t is_nan = mag + 0x01010101u;                 // bit 7 iff mag == 0x7F
-    const uint32_t exp_nz = mag + 0x78787878u;                 // bit 7 iff exponent != 0
-    const uint32_t man_nz = ((w & 0x07070707u) + 0x07070707u) << 4;  // bit 7 iff mantissa != 0
-    return (is_nan | (man_nz & ~exp_nz)) & 0x80808080u;
+    const uint32_t m = w & 0x7F7F7F7Fu;
+    const uint32_t ge1 = m + 0x7F7F7F7Fu, ge8 = m + 0x78787878u, nan = m + 0x01010101u;
+    return ((ge1 & ~ge8) | nan) & 0x80808080u;
 }
 
 // Four E4M3 codes (byte 0 first) -> four FP16 values in o0, o1.  Fast path:

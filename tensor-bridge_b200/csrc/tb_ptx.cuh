@@ -93,6 +93,19 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
     }
 }
 
+// One lane of the (converged) warp returns true.  Lets a whole warp run an
+// issue loop with warp-uniform values (kept in the uniform datapath) while a
+// single thread issues the TMA / tcgen05 instructions.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\t"
+        "elect.sync r|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // ---- proxy fences ---------------------------------------------------------------
 
 // Order this thread's generic-proxy shared-memory writes before later
@@ -223,6 +236,19 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t smem_byte_addr) {
     d |= static_cast<uint64_t>(1u) << 46;
     d |= static_cast<uint64_t>(2u) << 61;
     return d;
+}
+
+// The same descriptor split into its two 32-bit words: the low word holds the
+// start address (>> 4) and the leading byte offset, so advancing the start by
+// b bytes adds b >> 4 to it (shared addresses stay below 2^18, so the 14-bit
+// field does not carry); the high word is the same for every K-major
+// SWIZZLE_128B tile.
+__host__ __device__ constexpr uint32_t sdesc_lo(uint32_t smem_byte_addr) {
+    return ((smem_byte_addr >> 4) & 0x3FFFu) | (1u << 16);
+}
+constexpr uint32_t kSdescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint64_t sdesc_make(uint32_t lo) {
+    return (static_cast<uint64_t>(kSdescHi) << 32) | lo;
 }
 
 // Instruction descriptor (kind::f16 / kind::f8f6f4, dense): D format F32,

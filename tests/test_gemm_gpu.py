@@ -64,6 +64,7 @@ SHAPES = [
     (640, 16, 1024),     # 16 tokens
     (512, 128, 4096),    # 128 tokens, long K (split-K candidates)
     (130, 300, 96),
+    (256, 16, 16384),    # one tile column, 256 k-blocks: many ring phases per slot
 ]
 
 
@@ -125,6 +126,38 @@ def test_fused_equals_unfused_bitwise(tb, cuda, fmt):
     cuda.cuda.synchronize()
     unfused = from_dev(dD, np.float32).reshape(M, N)
     np.testing.assert_array_equal(fused.view(np.uint32), unfused.view(np.uint32))
+
+
+def run_unfused(tb, cuda, fmt, A, B16, M, N, K, alpha):
+    dA, dB = to_dev(cuda, A), to_dev(cuda, B16)
+    A16 = empty_dev(cuda, M * K * 2)
+    tb.decode(fmt, dA, A16, M * K)
+    dD = empty_dev(cuda, M * N * 4)
+    tb.gemm_f16(A16, dB, dD, M, N, K, alpha=alpha)
+    cuda.cuda.synchronize()
+    return from_dev(dD, np.float32).reshape(M, N)
+
+
+# Persistent CTAs walk several output tiles each once the tile count exceeds the
+# SM count (148 on B200): these shapes give every CTA 2 to 4 tiles, so the raw
+# and operand rings wrap across tile boundaries with TMA refills that hit L2.
+MULTI_TILE = [(4096, 4096, 4096), (2048, 4096, 512), (4096, 2304, 1024), (1024, 8192, 256)]
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1, O.BF16, O.TF32])
+@pytest.mark.parametrize("M,N,K", MULTI_TILE)
+def test_fused_multi_tile_per_cta(tb, cuda, fmt, M, N, K):
+    """Fused equals decode-then-GEMM bit for bit on every tile, and a band of
+    rows from each tile row agrees with the oracle."""
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=fmt * 13 + K)
+    fused = run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha, force_ws=False)
+    unfused = run_unfused(tb, cuda, fmt, A, B16, M, N, K, alpha)
+    bad = np.argwhere(fused.view(np.uint32) != unfused.view(np.uint32))
+    assert bad.size == 0, f"{len(bad)} mismatches, first tiles {sorted({(r // 128, c // 256) for r, c in bad[:64]})}"
+    for r0 in range(0, M, 1024):
+        rows = (r0 + 100, r0 + 164)  # straddles the boundary of two 128-row tiles
+        want = O.gemm(fmt, A, O.F16, B16, M, N, K, rows=rows, alpha=alpha)
+        check(fused[rows[0]:rows[1]], want)
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 256), (384, 200, 640), (128, 16, 2048)])
