@@ -164,6 +164,20 @@ tb_status tb_gemm_fused(tb_format a_fmt, const void* A, const uint16_t* B, void*
 /* Bytes of workspace tb_gemm_fused needs for this shape (0 if none). */
 size_t tb_gemm_fused_workspace(tb_format a_fmt, int M, int N, int K);
 
+/* No reference counterpart.  tb_gemm_fused without a workspace argument and
+ * without allocating: split-K partial sums go to a fixed 20 MiB array compiled
+ * into the library (one per device), for callers that may not allocate device
+ * memory themselves, such as plugins under a runtime that owns all HBM through
+ * its own pool and offers no workspace slot.  Shapes whose partial sums need
+ * more than 20 MiB (tb_gemm_fused_workspace > 20 MiB; none on a 148-SM B200)
+ * return TB_ERR_WORKSPACE.  The first call on each device does a one-time
+ * set-up (looks up the array's device address) and should come before any
+ * stream capture.  All calls on a device share the array, which keeps the last
+ * call's contents; calls that overlap in time on different streams race on it. */
+tb_status tb_gemm_fused_noalloc(tb_format a_fmt, const void* A, const uint16_t* B, void* D,
+                                int M, int N, int K, tb_out_type out, float alpha,
+                                tb_stream_t stream);
+
 /* Both operands quantized, run natively by tcgen05 kind::f8f6f4:
  * D = alpha * A * B^T with A [M x K] in a_fmt and B [N x K] in b_fmt, where
  * (a_fmt, b_fmt) is (E4M3, E4M3) or (E2M1_HW, E2M1_HW).  alpha is

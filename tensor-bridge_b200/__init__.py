@@ -94,6 +94,7 @@ SIGNATURES = {
     "tb_gemm_f16": (_st, [_p, _p, _p, _i, _i, _i, _i, _f, _p]),
     "tb_gemm_fused": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _sz, _p]),
     "tb_gemm_fused_workspace": (_sz, [_i, _i, _i, _i]),
+    "tb_gemm_fused_noalloc": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p]),
     "tb_gemm_native": (_st, [_i, _p, _i, _p, _p, _i, _i, _i, _i, _f, _p]),
     "tb_fp4_repack_hw": (_st, [_p, _p, _sz, _p]),
     "tb_gemm_fp8_fused_fp16": (_st, [_p, _p, _p, _i, _i, _i, _p, _sz, _p]),
@@ -189,6 +190,11 @@ def gemm_fused(fmt, A, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float =
                workspace_bytes: int = 0, stream=None):
     call("tb_gemm_fused", int(fmt), _ptr(A), _ptr(B), _ptr(D), M, N, K, int(out), alpha, _ptr(workspace),
          workspace_bytes, _stream(stream))
+
+
+def gemm_fused_noalloc(fmt, A, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):
+    """tb_gemm_fused with split-K partial sums in the library's fixed scratch."""
+    call("tb_gemm_fused_noalloc", int(fmt), _ptr(A), _ptr(B), _ptr(D), M, N, K, int(out), alpha, _stream(stream))
 
 
 def gemm_native(a_fmt, A, b_fmt, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):

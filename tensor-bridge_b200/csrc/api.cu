@@ -61,6 +61,10 @@ tb_status launch_gemm(const tb::GemmRequest& r, cudaStream_t st) {
 
 }  // namespace
 
+tb_status tb::set_last_error(tb_status s, const char* what, const char* detail) {
+    return fail(s, "%s: %s", what, detail);
+}
+
 extern "C" {
 
 const char* tb_status_string(tb_status s) {

@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include "tensor_bridge_b200.h"
 
 namespace tb {
 
@@ -47,6 +48,10 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
 // Device error word of the GEMM kernels (bounded-wait expiry).
 cudaError_t device_error_read(int* v);
 cudaError_t device_error_clear();
+
+// api.cu: record "<what>: <detail>" as the calling thread's last error and
+// return `s` (for entry points defined outside api.cu).
+tb_status set_last_error(tb_status s, const char* what, const char* detail);
 
 // Device properties cached per device.
 struct DeviceInfo {
