@@ -7,9 +7,13 @@ drawn from N(0, 0.02), per-tensor scale FORMAT_MAX/maxabs for FP8/FP4, B =
 FP16 activations from N(0, 1)):
     * the fused decode-in-shared-memory GEMM  D = alpha * decode(A) @ B^T
     * the unfused path: decode kernel to FP16 in HBM, then the tcgen05 GEMM
-and once the both-quantized case qA @ qB with E4M3 x E4M3 on the native
-kind::f8f6f4 tensor-core path; FP32 output, as the reference.  That is 9
-GEMMs of 2*4096^3 flops per step.  `value` is whole-job TFLOP/s.
+and the both-quantized case qA @ qB with E4M3 x E4M3 and E2M1 x E2M1 on the
+native kind::f8f6f4 tensor-core path; FP32 output, as the reference.  That is
+10 GEMMs of 2*4096^3 flops per step.  `value` is whole-job TFLOP/s.
+
+The same JSON line also carries, measured after the timed steps, the
+weight-only MLP shapes (W 14336x4096 and 4096x14336, 1-2048 tokens, GB/s
+against HBM) and the 8192^3 fused FP4 GEMM with FP16 output.
 
 On N GPUs (torchrun) every rank runs the same sweep on its own data (the
 sweep has no exchange step): weak scaling, value = all ranks' flops / the
@@ -194,16 +198,23 @@ class Sweep:
         self.b32 = b
         self.B16 = torch.empty(N * K * 2, dtype=torch.uint8, device=dev)
         tb.quantize(F.F16, b, self.B16, N * K)
-        # both-quantized case: B to E4M3 with its own per-tensor scale
+        # both-quantized case qA @ qB on kind::f8f6f4: B quantized with its own
+        # per-tensor scale; FP4 operands in the tensor core's nibble order
         tb.absmax(b, b.numel(), amax)
-        sb = float(np.float32(448.0) / np.float32(float(amax.item())))
-        self.B8 = torch.empty(N * K, dtype=torch.uint8, device=dev)
-        tb.quantize(F.E4M3, b, self.B8, N * K, scale=sb)
-        self.alpha_native = float(np.float32(1.0) / (np.float32(1.0 / self.alpha["e4m3"]) * np.float32(sb)))
+        bmax = float(amax.item())
+        self.native = {}
+        for name, f in (("e4m3", F.E4M3), ("e2m1", F.E2M1_HW)):
+            sb = float(np.float32(FORMAT_MAX[name]) / np.float32(bmax))
+            sa = float(np.float32(1.0) / np.float32(self.alpha[name]))
+            qa = torch.empty(tb.stored_bytes(f, M * K), dtype=torch.uint8, device=dev)
+            tb.quantize(f, self.a32[name], qa, M * K, scale=sa)
+            qb = torch.empty(tb.stored_bytes(f, N * K), dtype=torch.uint8, device=dev)
+            tb.quantize(f, b, qb, N * K, scale=sb)
+            self.native[name] = (f, qa, qb, float(np.float32(1.0) / (np.float32(sa) * np.float32(sb))))
         self.A16 = torch.empty(M * K * 2, dtype=torch.uint8, device=dev)
         self.Dfused = {n: torch.empty(M, N, dtype=torch.float32, device=dev) for n in FORMATS}
         self.Dunf = torch.empty(M, N, dtype=torch.float32, device=dev)
-        self.Dnat = torch.empty(M, N, dtype=torch.float32, device=dev)
+        self.Dnat = {n: torch.empty(M, N, dtype=torch.float32, device=dev) for n in self.native}
         self.flops_per_gemm = 2.0 * M * N * K
         self.launches = 0
 
@@ -218,9 +229,9 @@ class Sweep:
             out.append((f"decode_{name}", lambda f=f, A=A: tb.decode(f, A, self.A16, M * K)))
             out.append((f"gemm_after_{name}", lambda al=al: tb.gemm_f16(self.A16, self.B16, self.Dunf, M, N, K,
                                                                         out=tb.Out.F32, alpha=al)))
-        out.append(("native_e4m3", lambda: tb.gemm_native(tb.Format.E4M3, self.Aq["e4m3"], tb.Format.E4M3, self.B8,
-                                                          self.Dnat, M, N, K, out=tb.Out.F32,
-                                                          alpha=self.alpha_native)))
+        for name, (f, qa, qb, al) in self.native.items():
+            out.append((f"native_{name}", lambda f=f, qa=qa, qb=qb, al=al, name=name: tb.gemm_native(
+                f, qa, f, qb, self.Dnat[name], M, N, K, out=tb.Out.F32, alpha=al)))
         return out
 
     def gemm_flops(self, label: str) -> float:
@@ -280,11 +291,11 @@ def run_e2e(torch, tb, sw: Sweep, steps: int, warmup: int):
     M, N, K = sw.M, sw.N, sw.K
     hA = {n: sw.Aq[n].cpu().pin_memory() for n in FORMATS}
     hB16 = sw.B16.cpu().pin_memory()
-    hB8 = sw.B8.cpu().pin_memory()
+    hN = {n: (v[1].cpu().pin_memory(), v[2].cpu().pin_memory()) for n, v in sw.native.items()}
     hD = torch.empty(M, N, dtype=torch.float32).pin_memory()
     dA = torch.empty(max(a.numel() for a in sw.Aq.values()), dtype=torch.uint8, device="cuda")
     dB = torch.empty(sw.B16.numel(), dtype=torch.uint8, device="cuda")
-    dB8 = torch.empty(sw.B8.numel(), dtype=torch.uint8, device="cuda")
+    dB8 = torch.empty(max(v[2].numel() for v in sw.native.values()), dtype=torch.uint8, device="cuda")
     h2d = d2h = 0
 
     def step():
@@ -304,14 +315,14 @@ def run_e2e(torch, tb, sw: Sweep, steps: int, warmup: int):
             hD.copy_(sw.Dunf, non_blocking=True)
             h2d += 2 * (n + hB16.numel())
             d2h += 2 * hD.numel() * 4
-        n = hA["e4m3"].numel()
-        dA[:n].copy_(hA["e4m3"], non_blocking=True)
-        dB8.copy_(hB8, non_blocking=True)
-        tb.gemm_native(tb.Format.E4M3, dA, tb.Format.E4M3, dB8, sw.Dnat, M, N, K, out=tb.Out.F32,
-                       alpha=sw.alpha_native)
-        hD.copy_(sw.Dnat, non_blocking=True)
-        h2d += n + hB8.numel()
-        d2h += hD.numel() * 4
+        for name, (f, _, _, al) in sw.native.items():
+            ha, hb = hN[name]
+            dA[:ha.numel()].copy_(ha, non_blocking=True)
+            dB8[:hb.numel()].copy_(hb, non_blocking=True)
+            tb.gemm_native(f, dA, f, dB8, sw.Dnat[name], M, N, K, out=tb.Out.F32, alpha=al)
+            hD.copy_(sw.Dnat[name], non_blocking=True)
+            h2d += ha.numel() + hb.numel()
+            d2h += hD.numel() * 4
 
     for _ in range(warmup):
         step()
@@ -343,10 +354,93 @@ def quality(torch, tb, sw: Sweep, rows: int = 256):
         torch.cuda.synchronize()
         same = bool(torch.equal(sw.Dfused[name].view(torch.int32), sw.Dunf.view(torch.int32)))
         out[name] = {"rel_frob_vs_fp32": err, "fused_equals_unfused": same}
-    want = ref["e4m3"][r].double() @ sw.b32.double().T
-    out["native_e4m3"] = {"rel_frob_vs_fp32": float(torch.linalg.norm(sw.Dnat[r].double() - want) /
-                                                    torch.linalg.norm(want))}
+    for name in sw.native:
+        want = ref[name][r].double() @ sw.b32.double().T
+        out[f"native_{name}"] = {"rel_frob_vs_fp32": float(torch.linalg.norm(sw.Dnat[name][r].double() - want) /
+                                                           torch.linalg.norm(want))}
     return out
+
+
+# ---- the other configurations, reported beside the headline ----------------------------
+
+def time_each(torch, fn, iters: int, flush) -> float:
+    """Median device time (ms) of `fn`, one launch per CUDA-event pair with an
+    L2 flush between launches (outside the events)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in ev:
+        flush_l2(torch, flush)
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+
+def weights_q(torch, tb, fmt, rows: int, cols: int, std: float, seed: int):
+    """Seeded N(0, std) weights quantized with scale FORMAT_MAX / maxabs."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    a = torch.randn(rows, cols, generator=g, device="cuda") * std
+    amax = torch.zeros(1, dtype=torch.float32, device="cuda")
+    tb.absmax(a, a.numel(), amax)
+    fmax = 448.0 if fmt == tb.Format.E4M3 else 6.0
+    scale = float(np.float32(fmax) / np.float32(float(amax.item())))
+    q = torch.empty(tb.stored_bytes(fmt, rows * cols), dtype=torch.uint8, device="cuda")
+    tb.quantize(fmt, a, q, rows * cols, scale=scale)
+    return q, float(np.float32(1.0) / np.float32(scale))
+
+
+def mlp_weight_only(torch, tb, peaks, iters: int = 20):
+    """Weight-only inference shapes: W 14336 x 4096 and 4096 x 14336 (output
+    features x K) in E4M3 and packed E2M1, activations FP16 [tokens x K],
+    FP32 out, tokens 1/16/128/2048.  Fused decode-in-shared-memory GEMM
+    against decode kernel + GEMM.  Algorithmic bytes = stored W + X + D."""
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    out = []
+    for (M, K) in ((14336, 4096), (4096, 14336)):
+        for fname, fmt in (("e4m3", tb.Format.E4M3), ("e2m1", tb.Format.E2M1)):
+            A, alpha = weights_q(torch, tb, fmt, M, K, 0.02, seed=M + K + int(fmt))
+            A16 = torch.empty(M * K, dtype=torch.float16, device="cuda")
+            for N in (1, 16, 128, 2048):
+                g = torch.Generator(device="cuda")
+                g.manual_seed(N)
+                B = torch.randn(N, K, generator=g, device="cuda").half()
+                D = torch.empty(M, N, dtype=torch.float32, device="cuda")
+                wsb = tb.fused_workspace_bytes(fmt, M, N, K)
+                ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda")
+                fused = time_each(torch, lambda: tb.gemm_fused(fmt, A, B, D, M, N, K, alpha=alpha, workspace=ws,
+                                                               workspace_bytes=wsb), iters, flush)
+                dec = time_each(torch, lambda: tb.decode(fmt, A, A16, M * K), iters, flush)
+                gemm = time_each(torch, lambda: tb.gemm_f16(A16, B, D, M, N, K, alpha=alpha), iters, flush)
+                nbytes = A.numel() + N * K * 2 + M * N * 4
+                flops = 2.0 * M * N * K
+                out.append({"W": f"{M}x{K}", "fmt": fname, "tokens": N,
+                            "fused_us": fused * 1e3, "unfused_us": (dec + gemm) * 1e3,
+                            "fused_gbs": nbytes / fused / 1e6,
+                            "fused_pct_hbm": 100 * nbytes / fused / 1e6 / peaks["hbm_gbs"],
+                            "fused_tflops": flops / fused / 1e9, "fused_vs_unfused": (dec + gemm) / fused})
+            del A16
+    return out
+
+
+def fp4_square(torch, tb, peaks, n: int = 8192, iters: int = 10):
+    """Large square fused GEMM: A packed E2M1 from N(0, 1) with scale 6/maxabs,
+    B FP16 N(0, 1), FP32 accumulation, FP16 output."""
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    A, alpha = weights_q(torch, tb, tb.Format.E2M1, n, n, 1.0, seed=8192)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(8193)
+    B = torch.randn(n, n, generator=g, device="cuda").half()
+    D = torch.empty(n, n, dtype=torch.float16, device="cuda")
+    ms = time_each(torch, lambda: tb.gemm_fused(tb.Format.E2M1, A, B, D, n, n, n, out=tb.Out.F16, alpha=alpha),
+                   iters, flush)
+    tf = 2.0 * n ** 3 / ms / 1e9
+    return {"M": n, "N": n, "K": n, "fmt": "e2m1 packed", "out": "f16", "ms": ms, "tflops": tf,
+            "pct_f16_dense_peak_nominal": 100 * tf / 2250.0,
+            "frac_of_measured_bf16": tf / peaks["bf16_tflops"]}
 
 
 # ---- CPU baseline: the reference's own host path ---------------------------------------
@@ -463,6 +557,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--size", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the MLP-shape and 8192^3 FP4 sub-objects")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -498,9 +593,11 @@ def main():
             "decode_pct_hbm": 100 * sw.decode_bytes(name) / dec_ms / 1e6 / peaks["hbm_gbs"],
             **q[name],
         }
-    formats["native_e4m3"] = {"tflops": sw.flops_per_gemm / mean["native_e4m3"] / 1e9,
-                              "pct_fp8_dense_peak": 100 * sw.flops_per_gemm / mean["native_e4m3"] / 1e9 / 4500.0,
-                              **q["native_e4m3"]}
+    for name in sw.native:
+        # per-tensor FP4 goes through kind::f8f6f4 and runs at the FP8 rate
+        formats[f"native_{name}"] = {"tflops": sw.flops_per_gemm / mean[f"native_{name}"] / 1e9,
+                                     "pct_fp8_dense_peak": 100 * sw.flops_per_gemm / mean[f"native_{name}"] / 1e9
+                                     / 4500.0, **q[f"native_{name}"]}
     # dominant kernel: the kernel (instantiation) with the largest total time;
     # the four post-decode GEMMs are one kernel, the tcgen05 FP16 GEMM
     groups = {}
@@ -526,10 +623,10 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16xf16->f32 (decoded operands); e4m3xe4m3->f32 native",
+        "vs_baseline": None, "dtype": "f16xf16->f32 (decoded operands); e4m3xe4m3, e2m1xe2m1->f32 native",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
         "config": {"workload": f"format sweep {M}x{N}x{K}: fused + unfused decode+GEMM for TF32/BF16/E4M3/E2M1, "
-                               f"native E4M3xE4M3; FP32 out", "M": M, "N": N, "K": K,
+                               f"native E4M3xE4M3 and E2M1xE2M1; FP32 out", "M": M, "N": N, "K": K,
                    "gemms_per_step": len(sw.ops()) - len(FORMATS), "l2": "flushed between steps (256 MiB write)",
                    "parallelism": f"replicas x{dist.world}"},
         "roofline": roof,
@@ -539,6 +636,9 @@ def main():
         "clocks": clock,
         "formats": formats,
     }
+    if not args.no_extra:
+        line["weight_only_mlp"] = mlp_weight_only(torch, tb, peaks)
+        line["fp4_8192_fused"] = fp4_square(torch, tb, peaks)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline((M, N, K))
     dist.close()

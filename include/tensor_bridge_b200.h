@@ -178,13 +178,16 @@ tb_status tb_gemm_fused_noalloc(tb_format a_fmt, const void* A, const uint16_t* 
                                 int M, int N, int K, tb_out_type out, float alpha,
                                 tb_stream_t stream);
 
-/* Both operands quantized, run natively by tcgen05 kind::f8f6f4:
- * D = alpha * A * B^T with A [M x K] in a_fmt and B [N x K] in b_fmt, where
- * (a_fmt, b_fmt) is (E4M3, E4M3) or (E2M1_HW, E2M1_HW).  alpha is
- * 1/(scale_A*scale_B).  The tensor core reads E4M3 codes with exponent 0 as
- * subnormals where the reference decoder flushes them to zero; the
+/* Both operands quantized, run natively by tcgen05 kind::f8f6f4 (qA @ qB of
+ * bench/bench_formats.cu:140-150, without decoding to FP16):
+ * D = alpha * A * B^T with A [M x K] in a_fmt and B [N x K] in b_fmt, each of
+ * E4M3, E5M2 or E2M1_HW (mixed pairs allowed; with FP4, K % 128 == 0 and the
+ * FP4 operand 32-byte aligned).  alpha
+ * is 1/(scale_A*scale_B).  The tensor core reads E4M3 codes with exponent 0
+ * as subnormals where the reference decoder flushes them to zero; the
  * reference quantizer (fp32_to_fp8_e4m3, fp8.h:58) never emits such codes.
- * Use tb_fp4_repack_hw to turn reference-packed FP4 into TB_FMT_E2M1_HW. */
+ * Use tb_fp4_repack_hw to turn reference-packed FP4 into TB_FMT_E2M1_HW.
+ * FP4 runs at the FP8 rate here (per-tensor scale, no block scales). */
 tb_status tb_gemm_native(tb_format a_fmt, const void* A, tb_format b_fmt, const void* B, void* D,
                          int M, int N, int K, tb_out_type out, float alpha, tb_stream_t stream);
 

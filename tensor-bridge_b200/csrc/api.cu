@@ -246,18 +246,31 @@ tb_status tb_gemm_fused(tb_format a_fmt, const void* A, const uint16_t* B, void*
 
 tb_status tb_gemm_native(tb_format a_fmt, const void* A, tb_format b_fmt, const void* B, void* D, int M, int N, int K,
                          tb_out_type out, float alpha, tb_stream_t stream) {
-    if (!(a_fmt == TB_FMT_E4M3 && b_fmt == TB_FMT_E4M3))
-        return fail(TB_ERR_UNSUPPORTED, "native GEMM supports (E4M3, E4M3) in this build");
+    auto native_ok = [](tb_format f) { return f == TB_FMT_E4M3 || f == TB_FMT_E5M2 || f == TB_FMT_E2M1_HW; };
+    if (!native_ok(a_fmt) || !native_ok(b_fmt))
+        return fail(TB_ERR_UNSUPPORTED, "native GEMM operands must be E4M3, E5M2 or E2M1_HW (got %d, %d)", (int)a_fmt,
+                    (int)b_fmt);
     tb_status s = check_gemm_shape(M, N, K, a_fmt);
     if (s != TB_OK) return s;
+    s = check_gemm_shape(M, N, K, b_fmt);
+    if (s != TB_OK) return s;
+    // Packed FP4 reaches the tensor core through the 16U4_ALIGN16B tensor-map
+    // type, which needs a row length that is a multiple of 128 values and a
+    // 32-byte aligned base.
+    const bool fp4 = a_fmt == TB_FMT_E2M1_HW || b_fmt == TB_FMT_E2M1_HW;
+    if (fp4 && K % 128 != 0) return fail(TB_ERR_SHAPE, "native FP4 needs K %% 128 == 0 (got K = %d)", K);
     if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
     if (out != TB_OUT_F32 && out != TB_OUT_F16) return fail(TB_ERR_INVALID_ARGUMENT, "bad output type");
     if (!aligned16(A) || !aligned16(B)) return fail(TB_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+    if ((a_fmt == TB_FMT_E2M1_HW && (reinterpret_cast<uintptr_t>(A) & 31u)) ||
+        (b_fmt == TB_FMT_E2M1_HW && (reinterpret_cast<uintptr_t>(B) & 31u)))
+        return fail(TB_ERR_ALIGNMENT, "native FP4 operands must be 32-byte aligned");
     s = check_device();
     if (s != TB_OK) return s;
     tb::GemmRequest r{};
     r.kind = tb::GemmKind::kNative;
     r.a_fmt = a_fmt;
+    r.b_fmt = b_fmt;
     r.A = A; r.B = B; r.D = D; r.ldd = N;
     r.M = M; r.N = N; r.K = K;
     r.out_f16 = out == TB_OUT_F16;

@@ -89,6 +89,29 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tensor map of a native-mode operand [rows x K]: one 128-element k-block per
+// box row, 128-byte swizzle.  FP8 is one byte per element.  Packed FP4 (first
+// value in the low nibble) uses the 16U4_ALIGN16B type: TMA expands every 16
+// packed elements (8 bytes) to a 16-byte shared-memory chunk, the padded
+// layout kind::f8f6f4 reads 4-bit operands from, so a box row is again 128
+// bytes and the MMA descriptors match the FP8 case.
+static bool make_native_map(CUtensorMap* m, int fmt, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows) {
+    if (fmt == kE2M1HW)
+        return make_map(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, base, K, rows, K / 2, 128, box_rows,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, K, rows, K, 128, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// kind::f8f6f4 operand format codes of the instruction descriptor.
+static int f8f6f4_code(int fmt) {
+    switch (fmt) {
+        case kE4M3: return 0;
+        case kE5M2: return 1;
+        case kE2M1HW: return 5;
+        default: return -1;
+    }
+}
+
 // ---------------------------------------------------------------------------------
 // Configurations
 
@@ -172,8 +195,7 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
         ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, BN,
                             CU_TENSOR_MAP_SWIZZLE_128B);
     } else if constexpr (MODE == kModeNative8) {
-        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-        ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.B, K, r.N, K, 128, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+        ok = make_native_map(&ta, r.a_fmt, r.A, K, r.M, 128) && make_native_map(&tbm, r.b_fmt, r.B, K, r.N, BN);
     } else {
         // Raw A: 128-byte boxes, 128-byte swizzle (the decode warps read the
         // swizzled layout).
@@ -245,12 +267,20 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     const int vec_elems = r.out_f16 ? 8 : 4;
     a.vec_ok = ((reinterpret_cast<uintptr_t>(r.D) & 15u) == 0 && (r.ldd % vec_elems) == 0) ? 1 : 0;
     a.ws = splits > 1 ? static_cast<float*>(r.workspace) : nullptr;
+    if (r.kind == GemmKind::kNative) {
+        const int ca = f8f6f4_code(r.a_fmt), cb = f8f6f4_code(r.b_fmt);
+        if (ca < 0 || cb < 0) { *why = "native GEMM operands must be E4M3, E5M2 or E2M1_HW"; return cudaErrorInvalidValue; }
+        a.idesc_ab = (static_cast<uint32_t>(ca) << 7) | (static_cast<uint32_t>(cb) << 10);
+        // A TMA box of 16U4_ALIGN16B data credits the packed bytes it reads
+        // (64 per 128-value row), not the padded bytes it writes.
+        auto row_bytes = [](int f) { return f == kE2M1HW ? 64u : 128u; };
+        a.tx_bytes = 128u * row_bytes(r.a_fmt) + static_cast<uint32_t>(bn) * row_bytes(r.b_fmt);
+    }
 
     cudaError_t e;
     switch (r.kind) {
         case GemmKind::kF16: e = run_bn<kModeF16, kF16>(bn, r, a, st, dev, why); break;
         case GemmKind::kNative:
-            if (r.a_fmt != kE4M3) { *why = "native GEMM supports E4M3 x E4M3"; return cudaErrorInvalidValue; }
             if (bn == 16) e = run<16, kModeNative8, kE4M3>(r, a, st, dev, why);
             else if (bn == 64) e = run<64, kModeNative8, kE4M3>(r, a, st, dev, why);
             else if (bn == 128) e = run<128, kModeNative8, kE4M3>(r, a, st, dev, why);

@@ -134,8 +134,9 @@ struct GemmCfg {
     static constexpr int TMEM_COLS = pow2_at_least(2 * NACC * BN);
     static constexpr int CW = BN < 32 ? BN : 32;  // epilogue column chunk
 
-    // MMA: kind::f16 with FP16 operands, or kind::f8f6f4 with E4M3 (same
-    // format code 0), FP32 accumulation, K-major operands.
+    // MMA: kind::f16 with FP16 operands, or kind::f8f6f4 (operand formats
+    // OR'd in at run time from GemmArgs::idesc_ab), FP32 accumulation,
+    // K-major operands.
     static constexpr uint32_t IDESC = idesc_make(0u, 0u, BM, BN);
 
     // Decode work per k-block: 16-byte raw units per row and in total, and
@@ -164,6 +165,8 @@ struct GemmArgs {
     int out_f16;     // 1: FP16 output, 0: FP32
     int vec_ok;      // 1: D rows allow 16-byte vector stores
     float* ws;       // split-K partials [splits][M][N] (FP32), when splits > 1
+    uint32_t idesc_ab;  // native mode: A/B format fields of the instruction descriptor
+    uint32_t tx_bytes;  // native mode: TMA bytes per operand stage (packed FP4 counts 64 per 128-value row)
 };
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) ----------------------
@@ -408,7 +411,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             uint32_t ph = 0;
             long long issued = 0;
             bool ok = true;
-            constexpr uint32_t kTx = C::B_BYTES + (C::kDecode ? 0 : C::A_BYTES);
+            const uint32_t kTx =
+                C::MODE == kModeNative8 ? p.tx_bytes : C::B_BYTES + (C::kDecode ? 0u : static_cast<uint32_t>(C::A_BYTES));
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
                 int tm, tn, sp, kb0, kb1;
                 unit_coords(p, u, tm, tn, sp);
@@ -460,7 +464,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                             const uint32_t accum = (!first || kk >= C::NACC) ? 1u : 0u;
                             const uint32_t d = d_tmem + static_cast<uint32_t>((kk % C::NACC) * C::BN);
                             const uint64_t ad = sdesc_make(a_lo + 2u * kk), bd = sdesc_make(b_lo + 2u * kk);
-                            if constexpr (C::MODE == kModeNative8) mma_f8f6f4_ss(d, ad, bd, C::IDESC, accum);
+                            if constexpr (C::MODE == kModeNative8)
+                                mma_f8f6f4_ss(d, ad, bd, C::IDESC | p.idesc_ab, accum);
                             else mma_f16_ss(d, ad, bd, C::IDESC, accum);
                         }
                         mma_commit(&b_empty[bs]);

@@ -25,8 +25,9 @@ enum class GemmKind { kF16, kFused, kNative };
 struct GemmRequest {
     GemmKind kind;
     int a_fmt;          // stored format of A (decode / native) or kF16
+    int b_fmt;          // native: stored format of B (E4M3, E5M2 or E2M1_HW)
     const void* A;
-    const void* B;      // FP16 [N x K] (f16 / fused) or E4M3 [N x K] (native)
+    const void* B;      // FP16 [N x K] (f16 / fused) or b_fmt [N x K] (native)
     void* D;
     long long ldd;      // row stride of D in elements (normally N)
     int M, N, K;

@@ -61,6 +61,14 @@ def test_argument_validation_without_device(tb):
     # unsupported native pairing
     assert lib.tb_gemm_native(int(tb.Format.BF16), p, int(tb.Format.BF16), p, p, 64, 64, 64, 0, 1.0, null) == \
         tb.Status.UNSUPPORTED
+    # native FP4: K % 128 and 32-byte alignment
+    assert lib.tb_gemm_native(int(tb.Format.E2M1_HW), p, int(tb.Format.E2M1_HW), p, p, 64, 64, 96, 0, 1.0, null) == \
+        tb.Status.SHAPE
+    p16 = ctypes.c_void_p(256 + 16)
+    assert lib.tb_gemm_native(int(tb.Format.E4M3), p, int(tb.Format.E2M1_HW), p16, p, 64, 64, 128, 0, 1.0, null) == \
+        tb.Status.ALIGNMENT
+    assert lib.tb_gemm_native(int(tb.Format.E4M3), p, int(tb.Format.E2M1), p, p, 64, 64, 128, 0, 1.0, null) == \
+        tb.Status.UNSUPPORTED
     # fp8 mirror needs its workspace
     assert lib.tb_gemm_fp8_fused_fp16(p, p, p, 64, 64, 64, null, 0, null) == tb.Status.WORKSPACE
     assert lib.tb_gemm_fp8_fused_workspace(64, 48, 64) >= 48 * 64 * 2

@@ -175,6 +175,54 @@ def test_gemm_native_e4m3(tb, cuda, M, N, K):
     check(got, O.gemm(O.E4M3, A, O.E4M3, B, M, N, K, alpha=alpha))
 
 
+NATIVE_PAIRS = [(O.E2M1_HW, O.E2M1_HW), (O.E4M3, O.E2M1_HW), (O.E2M1_HW, O.E4M3), (O.E5M2, O.E5M2),
+                (O.E4M3, O.E5M2)]
+
+
+@pytest.mark.parametrize("fa,fb", NATIVE_PAIRS)
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (384, 200, 640), (128, 16, 2048), (1000, 72, 96)])
+def test_gemm_native_formats(tb, cuda, fa, fb, M, N, K):
+    """qA @ qB on kind::f8f6f4 for FP4 (16U4_ALIGN16B TMA expansion), E5M2
+    and mixed pairs, each operand with its own per-tensor scale."""
+    if O.E2M1_HW in (fa, fb) and K % 128:
+        pytest.skip("native FP4 needs K % 128 == 0")
+    a = O.normal(12, (M, K), 0.02)
+    b = O.normal(13, (N, K), 1.0)
+    sa, sb = O.per_tensor_scale(a, fa), O.per_tensor_scale(b, fb)
+    A, B = O.quantize(fa, a, sa), O.quantize(fb, b, sb)
+    alpha = float(np.float32(1.0) / (np.float32(sa) * np.float32(sb)))
+    dA, dB = to_dev(cuda, A), to_dev(cuda, B)
+    dD = empty_dev(cuda, M * N * 4)
+    tb.gemm_native(fa, dA, fb, dB, dD, M, N, K, alpha=alpha)
+    cuda.cuda.synchronize()
+    got = from_dev(dD, np.float32).reshape(M, N)
+    check(got, O.gemm(fa, A, fb, B, M, N, K, alpha=alpha))
+
+
+def test_native_fp4_matches_fused_after_repack(tb, cuda):
+    """Reference-packed FP4 weights repacked to the tensor-core nibble order
+    give the same product natively as the fused decode path does with FP16
+    activations that hold exactly the FP4 values."""
+    M, N, K = 512, 256, 1024
+    a, b = O.normal(14, (M, K), 1.0), O.normal(15, (N, K), 1.0)
+    sa, sb = O.per_tensor_scale(a, O.E2M1), O.per_tensor_scale(b, O.E2M1)
+    A_ref, B_ref = O.quantize(O.E2M1, a, sa), O.quantize(O.E2M1, b, sb)
+    dA, dB = to_dev(cuda, A_ref), to_dev(cuda, B_ref)
+    dA_hw, dB_hw = empty_dev(cuda, A_ref.nbytes), empty_dev(cuda, B_ref.nbytes)
+    tb.fp4_repack_hw(dA, dA_hw, A_ref.nbytes)
+    tb.fp4_repack_hw(dB, dB_hw, B_ref.nbytes)
+    dD = empty_dev(cuda, M * N * 4)
+    tb.gemm_native(tb.Format.E2M1_HW, dA_hw, tb.Format.E2M1_HW, dB_hw, dD, M, N, K)
+    B16 = empty_dev(cuda, N * K * 2)
+    tb.decode(tb.Format.E2M1, dB, B16, N * K)
+    dF = empty_dev(cuda, M * N * 4)
+    tb.gemm_fused(tb.Format.E2M1, dA, B16, dF, M, N, K)
+    cuda.cuda.synchronize()
+    native = from_dev(dD, np.float32).reshape(M, N)
+    fused = from_dev(dF, np.float32).reshape(M, N)
+    check(native, fused, tol=1e-6)
+
+
 def test_fp8_fused_fp16_mirror(tb, cuda):
     """tb_gemm_fp8_fused_fp16 mirrors gemm_fp8_fused_fp16: both operands E4M3,
     B given [K x N] row-major as the reference reads it."""
