@@ -6,6 +6,7 @@
 #include <mutex>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include "fused_tmem_kernel.cuh"
 #include "gemm_kernel.cuh"
 #include "tb_host.h"
 
@@ -220,8 +221,55 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
     return launch_cfg<C>(ta, tbm, args, st, dev);
 }
 
+// Narrow fused tiles: decoded A goes to TMEM (fused_tmem_kernel.cuh).  Raw
+// ring depth: as many stages (raw A box + its B tiles) as fit, up to eight.
+template <int BN, int FMT>
+struct PickTmem {
+    static constexpr int RSTAGE = raw_stage_bytes(FMT) + raw_kblocks(FMT) * BN * 128;
+    static constexpr int SR0 = (kSmemBudget - 1024) / RSTAGE;
+    static constexpr int SR = SR0 > 8 ? 8 : SR0;
+    using Cfg = TmemCfg<BN, FMT, SR>;
+};
+
+template <int BN, int FMT>
+static cudaError_t run_tmem(const GemmRequest& r, const GemmArgs& args, cudaStream_t st, int dev, const char** why) {
+    using C = typename PickTmem<BN, FMT>::Cfg;
+    CUtensorMap ta, tbm;
+    const uint64_t K = static_cast<uint64_t>(r.K);
+    constexpr uint32_t bx = raw_box_elems(FMT);
+    bool ok;
+    if constexpr (FMT == kE2M1) {
+        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K / 2, r.M, K / 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else if constexpr (FMT == kBF16) {
+        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else if constexpr (FMT == kTF32) {
+        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT32, r.A, K, r.M, K * 4, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!ok) {
+        *why = "cuTensorMapEncodeTiled rejected the operand layout";
+        return cudaErrorInvalidValue;
+    }
+    static std::atomic<uint64_t> attr_done{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_done.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(k_fused_tmem<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
+        if (e != cudaSuccess) return e;
+        attr_done.fetch_or(bit);
+    }
+    const int grid = std::min(args.num_units, device_info(dev).sms);
+    k_fused_tmem<C><<<grid, C::NUM_THREADS, C::SMEM_ALLOC, st>>>(ta, tbm, args);
+    return cudaGetLastError();
+}
+
 template <int MODE, int FMT>
 static cudaError_t run_bn(int bn, const GemmRequest& r, const GemmArgs& a, cudaStream_t st, int dev, const char** why) {
+    if constexpr (MODE == kModeDecode) {
+        if (bn == 16) return run_tmem<16, FMT>(r, a, st, dev, why);
+        if (bn == 64) return run_tmem<64, FMT>(r, a, st, dev, why);
+    }
     switch (bn) {
         case 16: return run<16, MODE, FMT>(r, a, st, dev, why);
         case 64: return run<64, MODE, FMT>(r, a, st, dev, why);
