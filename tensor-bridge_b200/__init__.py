@@ -210,3 +210,54 @@ def device_error(clear: bool = True) -> int:
     code = ctypes.c_int(0)
     call("tb_device_error", ctypes.byref(code), 1 if clear else 0)
     return code.value
+
+
+# ---- column-sharded weight GEMM (tb_gemm_sharded_fused) -------------------------------
+
+def shard_blocks(M: int, world: int, chunks: int, rank: int):
+    """Row blocks of a weight with M output rows that rank `rank` owns under the
+    block-cyclic layout of tb_gemm_sharded_fused: world*chunks blocks of
+    Mc = M / (world*chunks) rows; rank r owns blocks c*world + r, c < chunks.
+    Returns [(first_global_row, Mc), ...] in shard order."""
+    if M % (world * chunks * 128):
+        raise ValueError(f"M = {M} must be a multiple of world*chunks*128 = {world * chunks * 128}")
+    mc = M // (world * chunks)
+    return [((c * world + rank) * mc, mc) for c in range(chunks)]
+
+
+def shard_rows(A, M: int, world: int, chunks: int, rank: int):
+    """This rank's A_shard from the full weight A (numpy array or torch tensor
+    holding M rows of the stored format, any row width): its blocks stacked in
+    block order, as tb_gemm_sharded_fused expects."""
+    rows = A.reshape(M, -1)
+    parts = [rows[r0:r0 + mc] for r0, mc in shard_blocks(M, world, chunks, rank)]
+    if hasattr(rows, "new_empty"):  # torch
+        import torch
+        return torch.cat(parts).contiguous()
+    import numpy as np
+    return np.ascontiguousarray(np.concatenate(parts))
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    call("tb_nccl_unique_id", buf)
+    return buf.raw
+
+
+def nccl_comm_init(world: int, rank: int, uid: bytes) -> int:
+    """An ncclComm_t (as an int handle) for this rank, from rank 0's unique id."""
+    comm = ctypes.c_void_p()
+    call("tb_nccl_comm_init", ctypes.byref(comm), world, rank, ctypes.create_string_buffer(bytes(uid), 128))
+    return comm.value
+
+
+def nccl_comm_destroy(comm: int):
+    call("tb_nccl_comm_destroy", comm)
+
+
+def gemm_sharded_fused(fmt, A_shard, B, D, M: int, N: int, K: int, comm: int, chunks: int, out=Out.F32,
+                       alpha: float = 1.0, stream=None, comm_stream=None):
+    """Fused GEMM of this rank's block-cyclic weight rows straight into D, with
+    in-place NCCL all-gathers on comm_stream; every rank ends with all of D."""
+    call("tb_gemm_sharded_fused", int(fmt), _ptr(A_shard), _ptr(B), _ptr(D), M, N, K, int(out), alpha, comm,
+         chunks, _stream(stream), _ptr(comm_stream) if comm_stream is not None else _stream(None))

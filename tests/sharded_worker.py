@@ -1,0 +1,70 @@
+"""One rank of the 2-GPU sharded-GEMM test (launched by tests/test_sharded_gpu.py
+through torch.distributed.run).  gloo carries only the NCCL unique id; the
+GEMM's all-gather runs on the library's own NCCL communicator."""
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+sys.path.insert(0, ROOT)
+import oracle as O  # noqa: E402
+import __graft_entry__ as ge  # noqa: E402
+from gpu_util import to_dev, empty_dev, from_dev  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    tb = ge._import_package()
+    uid = torch.zeros(128, dtype=torch.uint8)
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(tb.nccl_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    comm = tb.nccl_comm_init(world, rank, bytes(uid.numpy()))
+    try:
+        for fmt, out, chunks, (M, N, K) in [(O.E4M3, tb.Out.F32, 2, (world * 2 * 128 * 3, 264, 512)),
+                                            (O.E2M1, tb.Out.F16, 3, (world * 3 * 128 * 2, 72, 1024))]:
+            a = O.normal(50 + fmt, (M, K), 0.02)
+            s = O.per_tensor_scale(a, fmt)
+            A = O.quantize(fmt, a, s)
+            alpha = float(np.float32(1.0) / np.float32(s))
+            B16 = O.f32_to_f16_bits(O.normal(51, (N, K), 1.0)).reshape(N, K)
+            esz = 2 if out == tb.Out.F16 else 4
+            dA_shard = to_dev(torch, tb.shard_rows(A, M, world, chunks, rank))
+            dA, dB = to_dev(torch, A), to_dev(torch, B16)
+            dD = empty_dev(torch, M * N * esz)
+            st, cst = torch.cuda.Stream(), torch.cuda.Stream()
+            torch.cuda.synchronize()
+            tb.gemm_sharded_fused(fmt, dA_shard, dB, dD, M, N, K, comm, chunks, out=out, alpha=alpha,
+                                  stream=st.cuda_stream, comm_stream=cst.cuda_stream)
+            st.synchronize()
+            cst.synchronize()
+            dR = empty_dev(torch, M * N * esz)
+            tb.gemm_fused(fmt, dA, dB, dR, M, N, K, out=out, alpha=alpha)
+            torch.cuda.synchronize()
+            got = from_dev(dD, np.uint8)
+            ref = from_dev(dR, np.uint8)
+            assert np.array_equal(got, ref), f"rank {rank}: sharded D differs from the unsharded fused GEMM"
+            rows = (M // 2 - 32, M // 2 + 32)
+            want = O.gemm(fmt, A, O.F16, B16, M, N, K, rows=rows, alpha=alpha, out_f16=out == tb.Out.F16)
+            g = got.view(np.uint16 if esz == 2 else np.float32).reshape(M, N)[rows[0]:rows[1]]
+            if esz == 2:
+                g, want = O.f16_bits_to_f32(g), O.f16_bits_to_f32(want)
+            err = O.rel_frob(g, want)
+            assert err <= 1e-3, f"rank {rank}: rel-Frobenius {err:.3e}"
+            assert tb.device_error() == 0
+        print(f"rank {rank} OK", flush=True)
+    finally:
+        tb.nccl_comm_destroy(comm)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
