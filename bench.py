@@ -13,7 +13,9 @@ native kind::f8f6f4 tensor-core path; FP32 output, as the reference.  That is
 
 The same JSON line also carries, measured after the timed steps, the
 weight-only MLP shapes (W 14336x4096 and 4096x14336, 1-2048 tokens, GB/s
-against HBM) and the 8192^3 fused FP4 GEMM with FP16 output.
+against HBM), the 8192^3 fused FP4 GEMM with FP16 output, and the
+16384x53248 E4M3 weight GEMM column-sharded over the N GPUs with an NCCL
+all-gather of the output (strong scaling).
 
 On N GPUs (torchrun) every rank runs the same sweep on its own data (the
 sweep has no exchange step): weak scaling, value = all ranks' flops / the
@@ -443,6 +445,67 @@ def fp4_square(torch, tb, peaks, n: int = 8192, iters: int = 10):
             "frac_of_measured_bf16": tf / peaks["bf16_tflops"]}
 
 
+def sharded_weight_gemm(torch, tb, dist, steps: int = 5, warmup: int = 2):
+    """The 16384 x 53248 E4M3 weight (N(0, 0.02), per-tensor scale 448/maxabs),
+    used as its transpose in the weight role: M = 53248 output rows, K = 16384;
+    X = 8192 FP16 tokens from N(0, 1), replicated; FP16 output.  On N GPUs the
+    output rows are split block-cyclically (4 chunks per rank), each rank runs
+    the fused kernel on its rows and NCCL all-gathers D in place, overlapped
+    chunk by chunk; on one GPU it is one fused GEMM.  Device time, max over ranks."""
+    M, N, K = 53248, 8192, 16384
+    world, rank = dist.world, dist.rank
+    chunks = 4 if world > 1 else 1
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    W = torch.randn(M, K, generator=g, device="cuda") * 0.02
+    amax = torch.zeros(1, dtype=torch.float32, device="cuda")
+    tb.absmax(W, W.numel(), amax)
+    scale = float(np.float32(448.0) / np.float32(float(amax.item())))
+    rows = W if world == 1 else tb.shard_rows(W, M, world, chunks, rank)
+    A = torch.empty(rows.numel(), dtype=torch.uint8, device="cuda")
+    tb.quantize(tb.Format.E4M3, rows, A, rows.numel(), scale=scale)
+    del W, rows
+    g.manual_seed(6)
+    X = torch.randn(N, K, generator=g, device="cuda").half()
+    D = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    alpha = float(np.float32(1.0) / np.float32(scale))
+    comm = None
+    st, cst = torch.cuda.Stream(), torch.cuda.Stream()
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(tb.nccl_unique_id()), dtype=torch.uint8))
+        dist.dist.broadcast(uid, 0)
+        comm = tb.nccl_comm_init(world, rank, bytes(uid.cpu().numpy()))
+
+    def step():
+        if comm is None:
+            tb.gemm_fused(tb.Format.E4M3, A, X, D, M, N, K, out=tb.Out.F16, alpha=alpha, stream=st.cuda_stream)
+        else:
+            tb.gemm_sharded_fused(tb.Format.E4M3, A, X, D, M, N, K, comm, chunks, out=tb.Out.F16, alpha=alpha,
+                                  stream=st.cuda_stream, comm_stream=cst.cuda_stream)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = dist.max(e0.elapsed_time(e1) / steps)
+    dist.barrier()
+    if comm is not None:
+        tb.nccl_comm_destroy(comm)
+    flops = 2.0 * M * N * K
+    return {"M": M, "N": N, "K": K, "fmt": "e4m3", "out": "f16", "world": world, "chunks": chunks,
+            "scaling": "strong", "ms": ms, "tflops_total": flops / ms / 1e9,
+            "tflops_per_gpu": flops / ms / 1e9 / world,
+            "allgather_bytes_per_rank": (world - 1) * (M // world) * N * 2 if world > 1 else 0}
+
+
 # ---- CPU baseline: the reference's own host path ---------------------------------------
 
 def cpu_baseline(sw_shape, seconds: float = 12.0):
@@ -639,6 +702,7 @@ def main():
     if not args.no_extra:
         line["weight_only_mlp"] = mlp_weight_only(torch, tb, peaks)
         line["fp4_8192_fused"] = fp4_square(torch, tb, peaks)
+        line["sharded_weight_gemm"] = sharded_weight_gemm(torch, tb, dist)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline((M, N, K))
     dist.close()
