@@ -82,13 +82,21 @@ struct TmemCfg {
     static_assert(BN == 16 || BN == 32 || BN == 64, "narrow tiles only");
     static_assert(RK <= NSLICE, "one k-block per slice per raw stage");
     static_assert(WPH == 32 || WPH == 16, "TMEM store width");
+    // PIPE: a decode warp holds back one k-block's t_full arrival while it
+    // waits for its next k-block of the same unit (NSLICE later).  The stages
+    // it waits on must not depend on that arrival: the MMA round (DK
+    // k-blocks) that frees its TMEM stage, and the one that frees the raw slot
+    // refilled for it, must both end before the held-back k-block.
+    // Off: measured slower for BF16 and no faster for the other formats.
+    static constexpr bool PIPE = false && TS >= NSLICE + DK && SR * RK >= NSLICE + RK + DK - 1;
     static_assert(A_COL0 + TS * 32 <= TMEM_COLS && TS >= NSLICE + DK, "TMEM budget");
+    static_assert(SR >= DK, "raw ring depth");
     static_assert(RA_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage alignment");
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
 // Decode one 16-byte raw unit into WPU words of FP16 pairs (lower K first).
-// `scalar` selects the reference-rule path for E4M3 / BF16 special codes.
+// `scalar` selects the reference-rule path for E4M3 / BF16 / TF32 special codes.
 template <int FMT>
 __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, bool scalar) {
     if constexpr (FMT == kE4M3) {
@@ -120,19 +128,26 @@ __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, 
             o[2] = decode_bf16_x2_fast(in.z); o[3] = decode_bf16_x2_fast(in.w);
         }
     } else if constexpr (FMT == kTF32) {
-        o[0] = decode_tf32_x2(in.x, in.y);
-        o[1] = decode_tf32_x2(in.z, in.w);
+        if (scalar) {
+            o[0] = decode_tf32_x2_scalar(in.x, in.y);
+            o[1] = decode_tf32_x2_scalar(in.z, in.w);
+        } else {
+            o[0] = decode_tf32_x2_fast(in.x, in.y);
+            o[1] = decode_tf32_x2_fast(in.z, in.w);
+        }
     }
 }
 
-// Nonzero if a unit holds a code the fast path does not reproduce (E4M3 /
-// BF16 only).
+// Nonzero if a unit holds a code the fast path does not reproduce (E4M3,
+// BF16, TF32).
 template <int FMT>
 __device__ __forceinline__ uint32_t unit_special_mask(const uint4& in) {
     if constexpr (FMT == kE4M3)
         return e4m3_special_mask(in.x) | e4m3_special_mask(in.y) | e4m3_special_mask(in.z) | e4m3_special_mask(in.w);
     else if constexpr (FMT == kBF16)
         return bf16_nan_lanes(in.x) | bf16_nan_lanes(in.y) | bf16_nan_lanes(in.z) | bf16_nan_lanes(in.w);
+    else if constexpr (FMT == kTF32)
+        return max(tf32_max_mag(in.x, in.y), tf32_max_mag(in.z, in.w)) >= kTf32ScalarFrom ? 1u : 0u;
     else
         return 0u;
 }
@@ -325,21 +340,28 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         }
     } else {
         // ---------------- decode warps: one k-block row slice -> FP16 words -> TMEM ----------------
+        // Software-pipelined where the ring depths allow it (PIPE): the
+        // completion wait of a k-block's TMEM stores (and its t_full arrival)
+        // comes after the barrier waits and raw loads of this warp's next
+        // k-block in the unit, so the store latency overlaps them.
         const int q = warp & 3;                          // TMEM lane quarter
         const int j = (warp - C::DECODE_WARP0) >> 2;     // k-block slice
         const int row = q * 32 + lane;                   // tile row owned by this thread
         const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(C::A_COL0);
-        long long g_raw = 0, g_t = 0;  // raw stages / k-blocks of the units before this one
+        int rs0 = 0, ts0 = 0;            // ring slots of the current unit's first raw stage / k-block
+        uint32_t rph0 = 0, tph0 = 0;
+        int pend_ts = -1;                // TMEM stage whose stores are in flight
         bool ok = true;
         for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
             int tm, tn, sp, kb0, kb1;
             unit_coords(p, u, tm, tn, sp);
             unit_kblocks(p, sp, kb0, kb1);
-            for (int kb = kb0 + j; kb < kb1; kb += C::NSLICE) {
-                const int i = kb - kb0;
-                const long long gr = g_raw + i / C::RK, gt = g_t + i;
-                const int rs = static_cast<int>(gr % C::SR), ts = static_cast<int>(gt % C::TS);
-                const uint32_t rph = static_cast<uint32_t>((gr / C::SR) & 1), tph = static_cast<uint32_t>((gt / C::TS) & 1);
+            const int nkb = kb1 - kb0;
+            for (int i = j; i < nkb; i += C::NSLICE) {
+                const int rsi = rs0 + i / C::RK, tsi = ts0 + i;
+                const int rs = rsi % C::SR, ts = tsi % C::TS;
+                const uint32_t rph = rph0 ^ static_cast<uint32_t>((rsi / C::SR) & 1);
+                const uint32_t tph = tph0 ^ static_cast<uint32_t>((tsi / C::TS) & 1);
                 const int sub = i % C::RK;
                 bool w_ok = mbar_wait(&raw_full[rs], rph, abort_flag);
                 w_ok = w_ok && mbar_wait(&t_empty[ts], tph ^ 1u, abort_flag);
@@ -352,8 +374,16 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                     uint4 in[C::UPH];
 #pragma unroll
                     for (int t = 0; t < C::UPH; ++t) in[t] = lds128(raw_unit_addr<C::FMT>(raw, sub, row, h * C::UPH + t));
+                    if (C::PIPE && h == 0 && pend_ts >= 0) {
+                        // The previous k-block's stores: complete, then publish.
+                        tmem_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&t_full[pend_ts]);
+                        pend_ts = -1;
+                    }
                     bool scalar = false;
-                    if constexpr (C::FMT == kE4M3 || C::FMT == kBF16) {
+                    if constexpr (C::FMT == kE4M3 || C::FMT == kBF16 || C::FMT == kTF32) {
                         uint32_t m = 0;
 #pragma unroll
                         for (int t = 0; t < C::UPH; ++t) m |= unit_special_mask<C::FMT>(in[t]);
@@ -370,13 +400,28 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                     if constexpr (C::WPH == 32) tmem_st_32x32b_x32(ta, *reinterpret_cast<const uint32_t(*)[32]>(o));
                     else tmem_st_32x32b_x16(ta + h * 16, *reinterpret_cast<const uint32_t(*)[16]>(o));
                 }
+                if constexpr (C::PIPE) {
+                    pend_ts = ts;
+                } else {
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&t_full[ts]);
+                }
+            }
+            if (pend_ts >= 0) {
+                // Publish the held-back k-block before the next unit.
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&t_full[ts]);
+                if (lane == 0 && ok) mbar_arrive(&t_full[pend_ts]);
+                pend_ts = -1;
             }
-            g_raw += (kb1 - kb0 + C::RK - 1) / C::RK;
-            g_t += kb1 - kb0;
+            const int nst = (nkb + C::RK - 1) / C::RK;
+            rph0 ^= static_cast<uint32_t>(((rs0 + nst) / C::SR) & 1);
+            rs0 = (rs0 + nst) % C::SR;
+            tph0 ^= static_cast<uint32_t>(((ts0 + nkb) / C::TS) & 1);
+            ts0 = (ts0 + nkb) % C::TS;
         }
     }
 

@@ -78,43 +78,40 @@ __device__ __forceinline__ void decode_e5m2_x4(uint32_t w, uint32_t& o0, uint32_
 }
 
 // ---- E2M1 ----------------------------------------------------------------------------
-// All 16 E2M1 values have FP16 encodings with a zero low byte, so the decode is
-// a byte table lookup on the 3-bit magnitude (one prmt over two constant words)
-// plus the sign bit.  High bytes for magnitudes 0..7:
-//   0x00 0x38 0x3C 0x3E | 0x40 0x42 0x44 0x46
-constexpr uint32_t kE2M1HiLo = 0x3E3C3800u;
-constexpr uint32_t kE2M1HiHi = 0x46444240u;
+// Every E2M1 value (0, 0.5, 1, 1.5, 2, 3, 4, 6 and their negatives, code 8
+// being -0) is an FP16 value, so the hardware conversion reproduces the
+// reference table (fp4.h:27-30) code for code.
+
+// Four bytes, each holding two E2M1 codes -> four FP16 pairs by the hardware
+// converter (cvt.rn.f16x2.e2m1x2: the low nibble of a byte becomes the low
+// half).  Exact for all 16 codes (code 8 is -0, as the reference table).
+__device__ __forceinline__ void cvt_e2m1x2_x4(uint32_t w, uint32_t (&o)[4]) {
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+        : "r"(w));
+}
 
 // Packed, reference order: byte j holds element 2j in its HIGH nibble and
-// element 2j+1 in its low nibble.  Eight elements -> o[0..3].
+// element 2j+1 in its low nibble.  Eight elements -> o[0..3]: swap the
+// nibbles of every byte (element 2j to the low half), then convert.
 __device__ __forceinline__ void decode_e2m1_packed_x8(uint32_t w, uint32_t (&o)[4]) {
-    const uint32_t mag = w & 0x77777777u;  // nibble k = magnitude of nibble k
-    // Byte k of hb0/hb1 = high FP16 byte of nibble k (k = 0..3 / 4..7).
-    const uint32_t hb0 = prmt(kE2M1HiLo, kE2M1HiHi, mag);
-    const uint32_t hb1 = prmt(kE2M1HiLo, kE2M1HiHi, mag >> 16);
-    // Sign of nibble k sits in bit 4k+3.  Odd nibbles (high halves of bytes)
-    // have it in a byte's bit 7; even nibbles after a 4-bit left shift.
-    const uint32_t ws = w << 4;
-    const uint32_t s0 = prmt(ws, w, 0xD9C8u);  // nibbles 0,1,2,3 -> 0x00/0xFF
-    const uint32_t s1 = prmt(ws, w, 0xFBEAu);  // nibbles 4,5,6,7
-    const uint32_t v0 = hb0 | (s0 & 0x80808080u);
-    const uint32_t v1 = hb1 | (s1 & 0x80808080u);
-    // Element order: e0 = nibble 1, e1 = nibble 0, e2 = nibble 3, e3 = nibble 2 ...
-    o[0] = prmt(v0, 0u, 0x0414u);  // {0, nib1, 0, nib0}
-    o[1] = prmt(v0, 0u, 0x2434u);  // {0, nib3, 0, nib2}
-    o[2] = prmt(v1, 0u, 0x0414u);
-    o[3] = prmt(v1, 0u, 0x2434u);
+    cvt_e2m1x2_x4(((w >> 4) & 0x0F0F0F0Fu) | ((w << 4) & 0xF0F0F0F0u), o);
 }
 
 // Unpacked (one value per byte, low nibble; high nibble ignored as in the
 // reference's `nibble & 0x0F`).  Four elements -> o0, o1.
 __device__ __forceinline__ void decode_e2m1_unpacked_x4(uint32_t w, uint32_t& o0, uint32_t& o1) {
-    const uint32_t mag = w & 0x07070707u;
-    const uint32_t sel = prmt(mag | (mag >> 4), 0u, 0x4420u);  // nibbles = magnitudes of bytes 0..3
-    const uint32_t hb = prmt(kE2M1HiLo, kE2M1HiHi, sel);
-    const uint32_t v = hb | ((w << 4) & 0x80808080u);         // bit 3 of each byte -> bit 7
-    o0 = prmt(v, 0u, 0x1404u);
-    o1 = prmt(v, 0u, 0x3424u);
+    const uint32_t t = w & 0x0F0F0F0Fu;
+    // byte 0 = code1 << 4 | code0, byte 2 = code3 << 4 | code2
+    uint32_t o[4];
+    cvt_e2m1x2_x4(t | (t >> 4), o);
+    o0 = o[0];
+    o1 = o[2];
 }
 
 // Tensor-core packing (element 2j in the LOW nibble): a nibble swap of the
@@ -170,8 +167,31 @@ __device__ __forceinline__ uint32_t decode_tf32_x1(uint32_t t) {
     return s | h;
 }
 
-__device__ __forceinline__ uint32_t decode_tf32_x2(uint32_t t0, uint32_t t1) {
+__device__ __forceinline__ uint32_t decode_tf32_x2_scalar(uint32_t t0, uint32_t t1) {
     return decode_tf32_x1(t0) | (decode_tf32_x1(t1) << 16);
+}
+
+// Largest magnitude of a pair; at or above 2^16 (0x47800000, which includes
+// Inf and NaN) a word needs the scalar path.
+__device__ __forceinline__ uint32_t tf32_max_mag(uint32_t t0, uint32_t t1) {
+    return max(t0 & 0x7FFFFFFFu, t1 & 0x7FFFFFFFu);
+}
+constexpr uint32_t kTf32ScalarFrom = 143u << 23;
+
+// Fast path, valid when both magnitudes are below 2^16.  Converting with
+// round-toward-zero drops the 13 low bits exactly as the reference's
+// truncation does and cannot round a value below 2^-14 up into the normal
+// range; FP16 subnormal results are then flushed to a signed zero (the
+// reference flushes every value below 2^-14).
+__device__ __forceinline__ uint32_t decode_tf32_x2_fast(uint32_t t0, uint32_t t1) {
+    uint32_t h;
+    asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(__uint_as_float(t1)), "f"(__uint_as_float(t0)));
+    const uint32_t normal = lane_mask_bit15((h & 0x7C007C00u) + 0x7C007C00u);
+    return h & (normal | 0x80008000u);
+}
+
+__device__ __forceinline__ uint32_t decode_tf32_x2(uint32_t t0, uint32_t t1) {
+    return tf32_max_mag(t0, t1) >= kTf32ScalarFrom ? decode_tf32_x2_scalar(t0, t1) : decode_tf32_x2_fast(t0, t1);
 }
 
 }  // namespace tb
