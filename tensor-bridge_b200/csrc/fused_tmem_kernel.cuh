@@ -13,47 +13,50 @@
 // weights and the small B tiles.
 //
 // Roles (one persistent CTA per SM, same work units as gemm_kernel.cuh):
-//   warp 0      TMA producer: one ring stage = the raw A box (RK k-blocks of
-//               128 rows) plus the RK B tiles of those k-blocks
+//   warp 0      TMA producer of the raw A ring: one stage = one raw A box (RK
+//               k-blocks of 128 rows)
 //   warp 1      TMEM allocator (all 512 columns) and MMA issuer
 //   warps 2-5   epilogue (as in gemm_kernel.cuh)
 //   warps 6-21  16 decode warps.  A warp may only touch the 32 TMEM lanes of
 //               its warp-id quarter q = warp % 4, so thread i owns tile row
 //               32 q + i.  Slice j = (warp - 6) / 4 of a quarter decodes the
-//               k-blocks kb0 + j, kb0 + j + 4, ... of each unit, whole rows of
-//               64 values, so four k-blocks are decoded at once and each warp
-//               waits only on its own k-block's stages.
+//               k-blocks whose CTA-wide index is j mod 4, whole rows of 64
+//               values, so four k-blocks are decoded at once.
+//   warp 22     TMA producer of the B ring: one B tile per k-block
 // TMEM columns: [0, ACC_COLS) two accumulators (NACC chains of BN columns
 // each), then TS A stages of 32 columns (64 FP16 values of K per lane).
 //
-// Barriers: raw_full (TMA bytes); raw_empty (4 * RK decode-warp arrivals --
-// the four quarters of each slice that reads one k-block of the stage, after
-// those raw words have been decoded -- plus one MMA commit after the stage's
-// last k-block, whose B tile the MMA reads in place; for a tail stage with
-// fewer than RK k-blocks the producer arrives for the missing slices);
-// t_full (4 arrivals once tcgen05.st has completed); t_empty (MMA commit);
-// acc_full / acc_empty as in gemm_kernel.cuh.  Every wait is bounded.
+// The raw A ring is released by the decode warps alone, as soon as they have
+// decoded their k-block of a stage, so weight loads stream independently of
+// the MMAs; B has its own ring that only the MMA consumes.  Each full barrier
+// is waited on only by the role whose arrivals free its slot, so no waiter can
+// see a slot refilled twice.  Barriers: raw_full (TMA bytes); raw_empty
+// (one arrival from each of the 16 decode warps, which all walk every stage);
+// b_full (TMA bytes) / b_empty (MMA commit); t_full (4 arrivals from the owner
+// slice once tcgen05.st has completed) / t_empty (MMA commit); acc_full /
+// acc_empty as in gemm_kernel.cuh.  Every wait is bounded.
 #pragma once
 
 #include "gemm_kernel.cuh"
 
 namespace tb {
 
-template <int BN_, int FMT_, int SR_>
+template <int BN_, int FMT_, int SR_, int SB_>
 struct TmemCfg {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
     static constexpr int FMT = FMT_;
     static constexpr int SR = SR_;   // raw ring stages
+    static constexpr int SB = SB_;   // B ring slots (one k-block's B tile each)
     static constexpr int NSLICE = 4; // decode warps per TMEM lane quarter
     static constexpr int ND = 4 * NSLICE;
     static constexpr int RK = raw_kblocks(FMT);
     static constexpr int RA_BYTES = raw_stage_bytes(FMT);
     static constexpr int B_BYTES = BN * 128;
-    static constexpr int RSTAGE_BYTES = RA_BYTES + RK * B_BYTES;
-    static constexpr int RAW_READERS = 4 * RK;  // decode warps reading one raw stage
+    static constexpr int RSTAGE_BYTES = RA_BYTES;
     static constexpr int DECODE_WARP0 = 6;
-    static constexpr int NUM_THREADS = (DECODE_WARP0 + ND) * 32;
+    static constexpr int B_WARP = DECODE_WARP0 + ND;  // TMA producer of the B ring
+    static constexpr int NUM_THREADS = (B_WARP + 1) * 32;
     static constexpr int DK = 4;     // k-blocks per MMA wait round
 
     static constexpr int NACC = BN <= 16 ? 4 : 2;
@@ -72,8 +75,9 @@ struct TmemCfg {
     static constexpr int WPH = 32 / H;
 
     static constexpr int OFF_R = 0;
-    static constexpr int OFF_BAR = OFF_R + SR * RSTAGE_BYTES;
-    static constexpr int NUM_BARS = 2 * SR + 2 * TS + 5;
+    static constexpr int OFF_B = OFF_R + SR * RSTAGE_BYTES;
+    static constexpr int OFF_BAR = OFF_B + SB * B_BYTES;
+    static constexpr int NUM_BARS = 2 * SR + 2 * SB + 2 * TS + 5;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
 
@@ -82,15 +86,9 @@ struct TmemCfg {
     static_assert(BN == 16 || BN == 32 || BN == 64, "narrow tiles only");
     static_assert(RK <= NSLICE, "one k-block per slice per raw stage");
     static_assert(WPH == 32 || WPH == 16, "TMEM store width");
-    // PIPE: a decode warp holds back one k-block's t_full arrival while it
-    // waits for its next k-block of the same unit (NSLICE later).  The stages
-    // it waits on must not depend on that arrival: the MMA round (DK
-    // k-blocks) that frees its TMEM stage, and the one that frees the raw slot
-    // refilled for it, must both end before the held-back k-block.
-    // Off: measured slower for BF16 and no faster for the other formats.
-    static constexpr bool PIPE = false && TS >= NSLICE + DK && SR * RK >= NSLICE + RK + DK - 1;
     static_assert(A_COL0 + TS * 32 <= TMEM_COLS && TS >= NSLICE + DK, "TMEM budget");
-    static_assert(SR >= DK, "raw ring depth");
+    static_assert(TS % NSLICE == 0, "each TMEM stage keeps one owner slice");
+    static_assert(SR >= DK && SB >= DK, "ring depths");
     static_assert(RA_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage alignment");
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
@@ -163,7 +161,9 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* raw_full = bars;
     uint64_t* raw_empty = raw_full + C::SR;
-    uint64_t* t_full = raw_empty + C::SR;
+    uint64_t* b_full = raw_empty + C::SR;
+    uint64_t* b_empty = b_full + C::SB;
+    uint64_t* t_full = b_empty + C::SB;
     uint64_t* t_empty = t_full + C::TS;
     uint64_t* acc_full = t_empty + C::TS;
     uint64_t* acc_empty = acc_full + 2;
@@ -177,7 +177,11 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::SR; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], C::RAW_READERS + 1);
+            mbar_init(&raw_empty[s], C::ND);
+        }
+        for (int s = 0; s < C::SB; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
         }
         for (int s = 0; s < C::TS; ++s) {
             mbar_init(&t_full[s], 4);
@@ -193,8 +197,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
     }
+    if (warp == C::B_WARP && lane == 0) tma_prefetch_desc(&tmB);
     if (warp == 1) {
         tmem_alloc(tmem_holder, C::TMEM_COLS);
         tmem_relinquish();
@@ -218,17 +222,12 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&raw_empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
                 const int nk = min(C::RK, kb1 - kb);
                 if (elect_one()) {
-                    // Slices with no k-block in a tail stage never read it.
-                    if (nk < C::RK) mbar_arrive_count(&raw_empty[s], 4u * static_cast<uint32_t>(C::RK - nk));
-                    mbar_arrive_expect_tx(&raw_full[s], C::RA_BYTES + nk * C::B_BYTES);
+                    mbar_arrive_expect_tx(&raw_full[s], C::RA_BYTES);
                     uint8_t* dst = smem + C::OFF_R + s * C::RSTAGE_BYTES;
                     const int x = kb * raw_elems_per_kblock(C::FMT);
                     tma_load_2d(dst, &tmA, &raw_full[s], x, tm * C::BM);
                     if constexpr (C::FMT == kTF32)
                         tma_load_2d(dst + 16384, &tmA, &raw_full[s], x + raw_box_elems(C::FMT), tm * C::BM);
-                    for (int j = 0; j < nk; ++j)
-                        tma_load_2d(dst + C::RA_BYTES + j * C::B_BYTES, &tmB, &raw_full[s], (kb + j) * 64,
-                                    tn * C::BN);
                 }
                 __syncwarp();
                 ++issued;
@@ -237,9 +236,9 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         }
         if (!ok && lane == 0) drain_ring(raw_full, C::SR, issued);
     } else if (warp == 1) {
-        // ---------------- MMA issuer: A from TMEM, B from the raw stage ----------------
-        int rs = 0, ts = 0;
-        uint32_t rph = 0, tph = 0;
+        // ---------------- MMA issuer: A from TMEM, B from the B ring ----------------
+        int bs = 0, ts = 0;
+        uint32_t bph = 0, tph = 0;
         int t = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x, ++t) {
@@ -253,25 +252,22 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::NACC * C::BN);
             for (int kb = kb0; kb < kb1; kb += C::DK) {
                 const int cnt = min(C::DK, kb1 - kb);
-                int tsd[C::DK], rsd[C::DK], subd[C::DK];
-                bool endd[C::DK];
+                int tsd[C::DK], bsd[C::DK];
                 bool w_ok = true;
                 {
-                    int r = rs, tt = ts;
-                    uint32_t rp = rph, tp = tph;
+                    int bb = bs, tt = ts;
+                    uint32_t bp = bph, tp = tph;
 #pragma unroll
                     for (int d = 0; d < C::DK; ++d) {
                         if (d < cnt) {
-                            const int sub = (kb + d - kb0) % C::RK;
-                            if (sub == 0) w_ok = w_ok && mbar_wait(&raw_full[r], rp, abort_flag);  // B tiles landed
-                            w_ok = w_ok && mbar_wait(&t_full[tt], tp, abort_flag);                 // A decoded
-                            tsd[d] = tt; rsd[d] = r; subd[d] = sub;
-                            endd[d] = sub + 1 == C::RK || kb + d + 1 == kb1;
+                            w_ok = w_ok && mbar_wait(&b_full[bb], bp, abort_flag);  // B tile landed
+                            w_ok = w_ok && mbar_wait(&t_full[tt], tp, abort_flag);  // A decoded
+                            tsd[d] = tt; bsd[d] = bb;
                             if (++tt == C::TS) { tt = 0; tp ^= 1u; }
-                            if (endd[d] && ++r == C::SR) { r = 0; rp ^= 1u; }
+                            if (++bb == C::SB) { bb = 0; bp ^= 1u; }
                         }
                     }
-                    rs = r; ts = tt; rph = rp; tph = tp;
+                    bs = bb; ts = tt; bph = bp; tph = tp;
                 }
                 if (!__all_sync(0xFFFFFFFFu, w_ok)) { ok = false; break; }
                 tc_fence_after();
@@ -280,8 +276,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                     for (int d = 0; d < C::DK; ++d) {
                         if (d < cnt) {
                             const bool first = kb + d == kb0;
-                            const uint32_t b_lo = sdesc_lo(sbase + C::OFF_R + rsd[d] * C::RSTAGE_BYTES + C::RA_BYTES +
-                                                           subd[d] * C::B_BYTES);
+                            const uint32_t b_lo = sdesc_lo(sbase + C::OFF_B + bsd[d] * C::B_BYTES);
                             const uint32_t a_t = tmem_base + static_cast<uint32_t>(C::A_COL0 + tsd[d] * 32);
 #pragma unroll
                             for (int kk = 0; kk < 4; ++kk) {
@@ -290,7 +285,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                                 mma_f16_ts(dd, a_t + 8u * kk, sdesc_make(b_lo + 2u * kk), C::IDESC, accum);
                             }
                             mma_commit(&t_empty[tsd[d]]);
-                            if (endd[d]) mma_commit(&raw_empty[rsd[d]]);
+                            mma_commit(&b_empty[bsd[d]]);
                         }
                     }
                 }
@@ -304,6 +299,28 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             mma_commit(fin_bar);
             mbar_wait_drain(fin_bar, 0u);
         }
+    } else if (warp == C::B_WARP) {
+        // ---------------- TMA producer: one B tile per k-block ----------------
+        int s = 0;
+        uint32_t ph = 0;
+        long long issued = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+            int tm, tn, sp, kb0, kb1;
+            unit_coords(p, u, tm, tn, sp);
+            unit_kblocks(p, sp, kb0, kb1);
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&b_empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(&b_full[s], C::B_BYTES);
+                    tma_load_2d(smem + C::OFF_B + s * C::B_BYTES, &tmB, &b_full[s], kb * 64, tn * C::BN);
+                }
+                __syncwarp();
+                ++issued;
+                if (++s == C::SB) { s = 0; ph ^= 1u; }
+            }
+        }
+        if (!ok && lane == 0) drain_ring(b_full, C::SB, issued);
     } else if (warp < 6) {
         // ---------------- epilogue ----------------
         const int quarter = warp & 3;
@@ -340,88 +357,73 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         }
     } else {
         // ---------------- decode warps: one k-block row slice -> FP16 words -> TMEM ----------------
-        // Software-pipelined where the ring depths allow it (PIPE): the
-        // completion wait of a k-block's TMEM stores (and its t_full arrival)
-        // comes after the barrier waits and raw loads of this warp's next
-        // k-block in the unit, so the store latency overlaps them.
+        // Every decode warp walks every raw stage in order: it waits for the
+        // stage, decodes the k-block of the stage that it owns (if any) and
+        // arrives on the stage's empty barrier, so no slot can be refilled
+        // before all sixteen warps have passed it.  The owner slice of a
+        // k-block is its CTA-wide index t mod 4; TS is a multiple of 4, so each
+        // TMEM stage is always written by the same four warps, which see every
+        // phase of its empty barrier in order.
         const int q = warp & 3;                          // TMEM lane quarter
-        const int j = (warp - C::DECODE_WARP0) >> 2;     // k-block slice
+        const int j = (warp - C::DECODE_WARP0) >> 2;     // slice: owns k-blocks with t % 4 == j
         const int row = q * 32 + lane;                   // tile row owned by this thread
         const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(C::A_COL0);
-        int rs0 = 0, ts0 = 0;            // ring slots of the current unit's first raw stage / k-block
-        uint32_t rph0 = 0, tph0 = 0;
-        int pend_ts = -1;                // TMEM stage whose stores are in flight
+        int rs = 0, ts = 0;              // raw slot of the next stage, TMEM stage of the next k-block
+        uint32_t rph = 0, tph = 0;
+        int t = 0;                       // CTA-wide k-block index
         bool ok = true;
         for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
             int tm, tn, sp, kb0, kb1;
             unit_coords(p, u, tm, tn, sp);
             unit_kblocks(p, sp, kb0, kb1);
-            const int nkb = kb1 - kb0;
-            for (int i = j; i < nkb; i += C::NSLICE) {
-                const int rsi = rs0 + i / C::RK, tsi = ts0 + i;
-                const int rs = rsi % C::SR, ts = tsi % C::TS;
-                const uint32_t rph = rph0 ^ static_cast<uint32_t>((rsi / C::SR) & 1);
-                const uint32_t tph = tph0 ^ static_cast<uint32_t>((tsi / C::TS) & 1);
-                const int sub = i % C::RK;
-                bool w_ok = mbar_wait(&raw_full[rs], rph, abort_flag);
-                w_ok = w_ok && mbar_wait(&t_empty[ts], tph ^ 1u, abort_flag);
-                if (!__all_sync(0xFFFFFFFFu, w_ok)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t raw = sbase + C::OFF_R + rs * C::RSTAGE_BYTES;
-                const uint32_t ta = t_lane + static_cast<uint32_t>(ts * 32);
+            for (int kb = kb0; kb < kb1; kb += C::RK) {
+                const int nk = min(C::RK, kb1 - kb);
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&raw_full[rs], rph, abort_flag))) { ok = false; break; }
+                // This warp's k-block in the stage: sub with (t + sub) % 4 == j (RK <= 4).
+                const int sub = (j - t) & 3;
+                if (sub < nk) {
+                    int tk = ts + sub;
+                    uint32_t tpk = tph;
+                    if (tk >= C::TS) { tk -= C::TS; tpk ^= 1u; }
+                    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&t_empty[tk], tpk ^ 1u, abort_flag))) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t raw = sbase + C::OFF_R + rs * C::RSTAGE_BYTES;
+                    const uint32_t ta = t_lane + static_cast<uint32_t>(tk * 32);
 #pragma unroll
-                for (int h = 0; h < C::H; ++h) {
-                    uint4 in[C::UPH];
+                    for (int h = 0; h < C::H; ++h) {
+                        uint4 in[C::UPH];
 #pragma unroll
-                    for (int t = 0; t < C::UPH; ++t) in[t] = lds128(raw_unit_addr<C::FMT>(raw, sub, row, h * C::UPH + t));
-                    if (C::PIPE && h == 0 && pend_ts >= 0) {
-                        // The previous k-block's stores: complete, then publish.
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&t_full[pend_ts]);
-                        pend_ts = -1;
+                        for (int x = 0; x < C::UPH; ++x)
+                            in[x] = lds128(raw_unit_addr<C::FMT>(raw, sub, row, h * C::UPH + x));
+                        bool scalar = false;
+                        if constexpr (C::FMT == kE4M3 || C::FMT == kBF16 || C::FMT == kTF32) {
+                            uint32_t m = 0;
+#pragma unroll
+                            for (int x = 0; x < C::UPH; ++x) m |= unit_special_mask<C::FMT>(in[x]);
+                            scalar = __any_sync(0xFFFFFFFFu, m != 0u);
+                        }
+                        uint32_t o[C::WPH];
+#pragma unroll
+                        for (int x = 0; x < C::UPH; ++x) decode_unit_words<C::FMT>(in[x], o + x * C::WPU, scalar);
+                        if constexpr (C::WPH == 32) tmem_st_32x32b_x32(ta, *reinterpret_cast<const uint32_t(*)[32]>(o));
+                        else tmem_st_32x32b_x16(ta + h * 16, *reinterpret_cast<const uint32_t(*)[16]>(o));
                     }
-                    bool scalar = false;
-                    if constexpr (C::FMT == kE4M3 || C::FMT == kBF16 || C::FMT == kTF32) {
-                        uint32_t m = 0;
-#pragma unroll
-                        for (int t = 0; t < C::UPH; ++t) m |= unit_special_mask<C::FMT>(in[t]);
-                        scalar = __any_sync(0xFFFFFFFFu, m != 0u);
-                    }
-                    uint32_t o[C::WPH];
-#pragma unroll
-                    for (int t = 0; t < C::UPH; ++t) decode_unit_words<C::FMT>(in[t], o + t * C::WPU, scalar);
-                    if (h == C::H - 1) {
-                        // This warp's raw words of the stage are consumed.
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&raw_empty[rs]);
-                    }
-                    if constexpr (C::WPH == 32) tmem_st_32x32b_x32(ta, *reinterpret_cast<const uint32_t(*)[32]>(o));
-                    else tmem_st_32x32b_x16(ta + h * 16, *reinterpret_cast<const uint32_t(*)[16]>(o));
-                }
-                if constexpr (C::PIPE) {
-                    pend_ts = ts;
-                } else {
+                    // The raw words are consumed (decoded above): release the stage.
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&t_full[ts]);
+                    if (lane == 0) mbar_arrive(&t_full[tk]);
+                } else {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
                 }
+                t += nk;
+                ts += nk;
+                if (ts >= C::TS) { ts -= C::TS; tph ^= 1u; }
+                if (++rs == C::SR) { rs = 0; rph ^= 1u; }
             }
-            if (pend_ts >= 0) {
-                // Publish the held-back k-block before the next unit.
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0 && ok) mbar_arrive(&t_full[pend_ts]);
-                pend_ts = -1;
-            }
-            const int nst = (nkb + C::RK - 1) / C::RK;
-            rph0 ^= static_cast<uint32_t>(((rs0 + nst) / C::SR) & 1);
-            rs0 = (rs0 + nst) % C::SR;
-            tph0 ^= static_cast<uint32_t>(((ts0 + nkb) / C::TS) & 1);
-            ts0 = (ts0 + nkb) % C::TS;
         }
     }
 

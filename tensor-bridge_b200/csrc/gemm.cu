@@ -221,14 +221,15 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
     return launch_cfg<C>(ta, tbm, args, st, dev);
 }
 
-// Narrow fused tiles: decoded A goes to TMEM (fused_tmem_kernel.cuh).  Raw
-// ring depth: as many stages (raw A box + its B tiles) as fit, up to eight.
+// Narrow fused tiles: decoded A goes to TMEM (fused_tmem_kernel.cuh).  The B
+// ring gets 16 (BN = 16) or 8 slots; the raw ring as many raw A boxes as fit
+// in the rest, up to twelve.
 template <int BN, int FMT>
 struct PickTmem {
-    static constexpr int RSTAGE = raw_stage_bytes(FMT) + raw_kblocks(FMT) * BN * 128;
-    static constexpr int SR0 = (kSmemBudget - 1024) / RSTAGE;
-    static constexpr int SR = SR0 > 8 ? 8 : SR0;
-    using Cfg = TmemCfg<BN, FMT, SR>;
+    static constexpr int SB = BN <= 16 ? 16 : 8;  // B slots (2 KB or 8 KB each)
+    static constexpr int SR0 = (kSmemBudget - 1024 - SB * BN * 128) / raw_stage_bytes(FMT);
+    static constexpr int SR = SR0 > 12 ? 12 : SR0;
+    using Cfg = TmemCfg<BN, FMT, SR, SB>;
 };
 
 template <int BN, int FMT>

@@ -65,6 +65,10 @@ SHAPES = [
     (512, 128, 4096),    # 128 tokens, long K (split-K candidates)
     (130, 300, 96),
     (256, 16, 16384),    # one tile column, 256 k-blocks: many ring phases per slot
+    (512, 40, 2048),     # 17..64 tokens
+    (1000, 64, 1536),
+    (300, 24, 4160),     # ragged M, K with a partial raw stage
+    (256, 8, 80),
 ]
 
 
