@@ -395,17 +395,43 @@ def weights_q(torch, tb, fmt, rows: int, cols: int, std: float, seed: int):
     return q, float(np.float32(1.0) / np.float32(scale))
 
 
-def mlp_weight_only(torch, tb, peaks, iters: int = 20):
+def time_rotating(torch, fns, iters: int) -> float:
+    """Median device time (ms) per launch of a back-to-back sequence: each
+    iteration launches every callable of `fns` once, in order, between one
+    CUDA-event pair, and the time is divided by len(fns).  The callables work
+    on distinct buffers whose total is larger than the 126 MB L2, so every
+    launch reads its inputs from HBM, as consecutive layers of a model do; no
+    per-launch event or host gap is inside the figure."""
+    stream = torch.cuda.current_stream()
+    for fn in fns:
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in ev:
+        a.record(stream)
+        for fn in fns:
+            fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in ev) / len(fns)
+
+
+ROTATE_BYTES = 400_000_000  # > 3 x L2
+
+
+def mlp_weight_only(torch, tb, peaks, iters: int = 10):
     """Weight-only inference shapes: W 14336 x 4096 and 4096 x 14336 (output
     features x K) in E4M3 and packed E2M1, activations FP16 [tokens x K],
     FP32 out, tokens 1/16/128/2048.  Fused decode-in-shared-memory GEMM
-    against decode kernel + GEMM.  Algorithmic bytes = stored W + X + D."""
-    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    against decode kernel + GEMM.  Each figure is per launch of a back-to-back
+    sequence over C copies of the weight (C x stored bytes > 400 MB, so every
+    launch streams its weight from HBM).  Algorithmic bytes = stored W + X + D."""
     out = []
     for (M, K) in ((14336, 4096), (4096, 14336)):
         for fname, fmt in (("e4m3", tb.Format.E4M3), ("e2m1", tb.Format.E2M1)):
             A, alpha = weights_q(torch, tb, fmt, M, K, 0.02, seed=M + K + int(fmt))
-            A16 = torch.empty(M * K, dtype=torch.float16, device="cuda")
+            copies = max(2, -(-ROTATE_BYTES // A.numel()))
+            As = [A] + [A.clone() for _ in range(copies - 1)]
+            A16 = [torch.empty(M * K, dtype=torch.float16, device="cuda") for _ in range(2)]
             for N in (1, 16, 128, 2048):
                 g = torch.Generator(device="cuda")
                 g.manual_seed(N)
@@ -413,18 +439,49 @@ def mlp_weight_only(torch, tb, peaks, iters: int = 20):
                 D = torch.empty(M, N, dtype=torch.float32, device="cuda")
                 wsb = tb.fused_workspace_bytes(fmt, M, N, K)
                 ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda")
-                fused = time_each(torch, lambda: tb.gemm_fused(fmt, A, B, D, M, N, K, alpha=alpha, workspace=ws,
-                                                               workspace_bytes=wsb), iters, flush)
-                dec = time_each(torch, lambda: tb.decode(fmt, A, A16, M * K), iters, flush)
-                gemm = time_each(torch, lambda: tb.gemm_f16(A16, B, D, M, N, K, alpha=alpha), iters, flush)
+                fused = time_rotating(torch, [lambda Ai=Ai: tb.gemm_fused(fmt, Ai, B, D, M, N, K, alpha=alpha,
+                                                                          workspace=ws, workspace_bytes=wsb)
+                                              for Ai in As], iters)
+                dec = time_rotating(torch, [lambda i=i, Ai=Ai: tb.decode(fmt, Ai, A16[i & 1], M * K)
+                                            for i, Ai in enumerate(As)], iters)
+                gemm = time_rotating(torch, [lambda i=i: tb.gemm_f16(A16[i & 1], B, D, M, N, K, alpha=alpha)
+                                             for i in range(copies)], iters)
                 nbytes = A.numel() + N * K * 2 + M * N * 4
                 flops = 2.0 * M * N * K
-                out.append({"W": f"{M}x{K}", "fmt": fname, "tokens": N,
+                out.append({"W": f"{M}x{K}", "fmt": fname, "tokens": N, "weight_copies": copies,
                             "fused_us": fused * 1e3, "unfused_us": (dec + gemm) * 1e3,
                             "fused_gbs": nbytes / fused / 1e6,
                             "fused_pct_hbm": 100 * nbytes / fused / 1e6 / peaks["hbm_gbs"],
                             "fused_tflops": flops / fused / 1e9, "fused_vs_unfused": (dec + gemm) / fused})
-            del A16
+            del A16, As
+    return out
+
+
+def decode_streams(torch, tb, peaks, rows: int = 14336, cols: int = 4096, iters: int = 10):
+    """The standalone decode streamers on a 14336 x 4096 weight per format
+    (N(0, 0.02) quantized per tensor): per launch of a back-to-back sequence
+    alternating over two (input, output) pairs, 2 x (stored + FP16) bytes >
+    L2.  Algorithmic bytes = stored bytes read + FP16 bytes written."""
+    n = rows * cols
+    out = {}
+    F = tb.Format
+    for name, fmt in (("tf32", F.TF32), ("bf16", F.BF16), ("e4m3", F.E4M3), ("e2m1", F.E2M1)):
+        if name in FORMAT_MAX:
+            A, _ = weights_q(torch, tb, fmt, rows, cols, 0.02, seed=7 + int(fmt))
+        else:
+            g = torch.Generator(device="cuda")
+            g.manual_seed(7 + int(fmt))
+            a = torch.randn(rows, cols, generator=g, device="cuda") * 0.02
+            A = torch.empty(tb.stored_bytes(fmt, n), dtype=torch.uint8, device="cuda")
+            tb.quantize(fmt, a, A, n)
+            del a
+        pairs = [(A, torch.empty(n, dtype=torch.float16, device="cuda")),
+                 (A.clone(), torch.empty(n, dtype=torch.float16, device="cuda"))]
+        ms = time_rotating(torch, [lambda s=s, d=d: tb.decode(fmt, s, d, n) for s, d in pairs] * 2, iters)
+        nbytes = A.numel() + 2 * n
+        out[name] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                     "pct_hbm": 100 * nbytes / ms / 1e6 / peaks["hbm_gbs"]}
+        del pairs, A
     return out
 
 
@@ -700,6 +757,7 @@ def main():
         "formats": formats,
     }
     if not args.no_extra:
+        line["decode_stream_14336x4096"] = decode_streams(torch, tb, peaks)
         line["weight_only_mlp"] = mlp_weight_only(torch, tb, peaks)
         line["fp4_8192_fused"] = fp4_square(torch, tb, peaks)
         line["sharded_weight_gemm"] = sharded_weight_gemm(torch, tb, dist)

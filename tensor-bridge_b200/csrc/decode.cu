@@ -2,9 +2,10 @@
 //
 // These replace the reference's one-element-per-thread decode kernels
 // (src/gemm.cu:25-30, bench/bench_formats.cu:33-56).  The straight kernel is
-// a grid-stride HBM streamer: each thread step loads 16-byte input units with
-// 128-bit loads and writes the decoded FP16 with 128-bit stores, two units in
-// flight per thread.  The transposed kernel (the reference's B operand,
+// a grid-stride HBM streamer: each warp step reads 32 x kRep consecutive
+// items (4-16 bytes each, one load per item) and writes their decoded FP16
+// chunks (8 or 16 bytes, one store per item), kRep items in flight per thread,
+// so every warp-wide load and store covers whole contiguous 32-byte sectors.  The transposed kernel (the reference's B operand,
 // B16[col*K + k] = decode(B[k*N + col])) goes through a 32 x 64 shared-memory
 // tile so both the reads and the writes are coalesced.
 #include <cstdint>
@@ -15,42 +16,40 @@
 
 namespace tb {
 
-// Per-format geometry of one 16-byte input unit.
-template <int FMT> struct Unit;
-template <> struct Unit<kE4M3> { static constexpr int kIn = 1, kOut = 2, kElems = 16; };
-template <> struct Unit<kE5M2> { static constexpr int kIn = 1, kOut = 2, kElems = 16; };
-template <> struct Unit<kE2M1U> { static constexpr int kIn = 1, kOut = 2, kElems = 16; };
-template <> struct Unit<kE2M1> { static constexpr int kIn = 1, kOut = 4, kElems = 32; };
-template <> struct Unit<kBF16> { static constexpr int kIn = 1, kOut = 1, kElems = 8; };
-template <> struct Unit<kTF32> { static constexpr int kIn = 2, kOut = 1, kElems = 8; };
-template <> struct Unit<kF16> { static constexpr int kIn = 1, kOut = 1, kElems = 8; };
+// Per-format geometry of one item: the input bytes that decode to one output
+// chunk.  Every item is a single aligned load and a single aligned store, and
+// the 32 lanes of a warp touch 32 consecutive items, so both the loads and the
+// stores of a warp are contiguous (no half-written 32-byte sectors).
+template <int FMT> struct Item;
+template <> struct Item<kE4M3> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
+template <> struct Item<kE5M2> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
+template <> struct Item<kE2M1U> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
+template <> struct Item<kE2M1> { using In = uint32_t; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
+template <> struct Item<kBF16> { using In = uint4; using Out = uint4; static constexpr int kElems = 8, kRep = 4; };
+template <> struct Item<kTF32> { using In = uint4; using Out = uint2; static constexpr int kElems = 4, kRep = 4; };
+template <> struct Item<kF16> { using In = uint4; using Out = uint4; static constexpr int kElems = 8, kRep = 4; };
 
 template <int FMT>
-__device__ __forceinline__ void decode_vec(const uint4 (&in)[Unit<FMT>::kIn], uint4 (&out)[Unit<FMT>::kOut]) {
+__device__ __forceinline__ typename Item<FMT>::Out decode_item(const typename Item<FMT>::In& in) {
+    typename Item<FMT>::Out out;
     if constexpr (FMT == kE4M3) {
-        decode_e4m3_x4(in[0].x, out[0].x, out[0].y); decode_e4m3_x4(in[0].y, out[0].z, out[0].w);
-        decode_e4m3_x4(in[0].z, out[1].x, out[1].y); decode_e4m3_x4(in[0].w, out[1].z, out[1].w);
+        decode_e4m3_x4(in.x, out.x, out.y); decode_e4m3_x4(in.y, out.z, out.w);
     } else if constexpr (FMT == kE5M2) {
-        decode_e5m2_x4(in[0].x, out[0].x, out[0].y); decode_e5m2_x4(in[0].y, out[0].z, out[0].w);
-        decode_e5m2_x4(in[0].z, out[1].x, out[1].y); decode_e5m2_x4(in[0].w, out[1].z, out[1].w);
+        decode_e5m2_x4(in.x, out.x, out.y); decode_e5m2_x4(in.y, out.z, out.w);
     } else if constexpr (FMT == kE2M1U) {
-        decode_e2m1_unpacked_x4(in[0].x, out[0].x, out[0].y); decode_e2m1_unpacked_x4(in[0].y, out[0].z, out[0].w);
-        decode_e2m1_unpacked_x4(in[0].z, out[1].x, out[1].y); decode_e2m1_unpacked_x4(in[0].w, out[1].z, out[1].w);
+        decode_e2m1_unpacked_x4(in.x, out.x, out.y); decode_e2m1_unpacked_x4(in.y, out.z, out.w);
     } else if constexpr (FMT == kE2M1) {
         uint32_t o[4];
-        decode_e2m1_packed_x8(in[0].x, o); out[0] = make_uint4(o[0], o[1], o[2], o[3]);
-        decode_e2m1_packed_x8(in[0].y, o); out[1] = make_uint4(o[0], o[1], o[2], o[3]);
-        decode_e2m1_packed_x8(in[0].z, o); out[2] = make_uint4(o[0], o[1], o[2], o[3]);
-        decode_e2m1_packed_x8(in[0].w, o); out[3] = make_uint4(o[0], o[1], o[2], o[3]);
+        decode_e2m1_packed_x8(in, o);
+        out = make_uint4(o[0], o[1], o[2], o[3]);
     } else if constexpr (FMT == kBF16) {
-        out[0] = make_uint4(decode_bf16_x2(in[0].x), decode_bf16_x2(in[0].y), decode_bf16_x2(in[0].z),
-                            decode_bf16_x2(in[0].w));
+        out = make_uint4(decode_bf16_x2(in.x), decode_bf16_x2(in.y), decode_bf16_x2(in.z), decode_bf16_x2(in.w));
     } else if constexpr (FMT == kTF32) {
-        out[0] = make_uint4(decode_tf32_x2(in[0].x, in[0].y), decode_tf32_x2(in[0].z, in[0].w),
-                            decode_tf32_x2(in[1].x, in[1].y), decode_tf32_x2(in[1].z, in[1].w));
+        out = make_uint2(decode_tf32_x2(in.x, in.y), decode_tf32_x2(in.z, in.w));
     } else {
-        out[0] = in[0];
+        out = in;
     }
+    return out;
 }
 
 // Scalar decode of element i (used for tails and misaligned buffers).
@@ -67,39 +66,37 @@ __device__ __forceinline__ uint16_t decode_at(const void* src, size_t i) {
     else return static_cast<const uint16_t*>(src)[i];
 }
 
+// Grid-stride over warp chunks of 32 x kRep consecutive items.  Each thread
+// issues its kRep loads (lane, lane + 32, ...) before any decode, then stores
+// the kRep outputs; the last partial chunk is bounds-checked per item.
 template <int FMT>
-__global__ void __launch_bounds__(256) k_decode_stream(const uint4* __restrict__ src, uint4* __restrict__ dst,
-                                                       size_t units, const void* __restrict__ tail_src,
+__global__ void __launch_bounds__(256) k_decode_stream(const typename Item<FMT>::In* __restrict__ src,
+                                                       typename Item<FMT>::Out* __restrict__ dst, size_t items,
+                                                       const void* __restrict__ tail_src,
                                                        uint16_t* __restrict__ tail_dst, size_t tail_begin,
                                                        size_t n) {
-    using U = Unit<FMT>;
-    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-    size_t u = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    // Two units per thread per step: both loads are issued before either decode.
-    for (; u + stride < units; u += 2 * stride) {
-        uint4 a[U::kIn], b[U::kIn];
+    using I = Item<FMT>;
+    constexpr size_t kChunk = 32 * I::kRep;
+    const int lane = threadIdx.x & 31;
+    const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const size_t nwarps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+    for (size_t base = warp * kChunk; base < items; base += nwarps * kChunk) {
+        typename I::In in[I::kRep];
+        if (base + kChunk <= items) {
 #pragma unroll
-        for (int j = 0; j < U::kIn; ++j) a[j] = __ldcs(src + u * U::kIn + j);
+            for (int j = 0; j < I::kRep; ++j) in[j] = __ldcs(src + base + j * 32 + lane);
 #pragma unroll
-        for (int j = 0; j < U::kIn; ++j) b[j] = __ldcs(src + (u + stride) * U::kIn + j);
-        uint4 oa[U::kOut], ob[U::kOut];
-        decode_vec<FMT>(a, oa);
-        decode_vec<FMT>(b, ob);
+            for (int j = 0; j < I::kRep; ++j) dst[base + j * 32 + lane] = decode_item<FMT>(in[j]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < U::kOut; ++j) dst[u * U::kOut + j] = oa[j];
+            for (int j = 0; j < I::kRep; ++j)
+                if (base + j * 32 + lane < items) in[j] = __ldcs(src + base + j * 32 + lane);
 #pragma unroll
-        for (int j = 0; j < U::kOut; ++j) dst[(u + stride) * U::kOut + j] = ob[j];
+            for (int j = 0; j < I::kRep; ++j)
+                if (base + j * 32 + lane < items) dst[base + j * 32 + lane] = decode_item<FMT>(in[j]);
+        }
     }
-    if (u < units) {
-        uint4 a[U::kIn];
-#pragma unroll
-        for (int j = 0; j < U::kIn; ++j) a[j] = __ldcs(src + u * U::kIn + j);
-        uint4 oa[U::kOut];
-        decode_vec<FMT>(a, oa);
-#pragma unroll
-        for (int j = 0; j < U::kOut; ++j) dst[u * U::kOut + j] = oa[j];
-    }
-    // Elements past the last whole unit (fewer than one unit).
+    // Elements past the last whole item (fewer than one item).
     const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (tail_begin + gt < n) tail_dst[tail_begin + gt] = decode_at<FMT>(tail_src, tail_begin + gt);
 }
@@ -185,20 +182,21 @@ static size_t in_bytes_of(int fmt, size_t n) {
 
 template <int FMT>
 static cudaError_t launch_decode(const void* src, uint16_t* dst, size_t n, cudaStream_t st, int sms) {
-    using U = Unit<FMT>;
+    using I = Item<FMT>;
     const bool aligned = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0;
     if (!aligned) {
         const size_t blocks = std::min<size_t>((n + 255) / 256, static_cast<size_t>(sms) * 8);
         k_decode_scalar<FMT><<<static_cast<unsigned>(std::max<size_t>(blocks, 1)), 256, 0, st>>>(src, dst, n);
         return cudaGetLastError();
     }
-    const size_t units = n / U::kElems;
-    const size_t tail_begin = units * U::kElems;
-    const size_t want = (units + 255) / 256;
+    const size_t items = n / I::kElems;
+    const size_t tail_begin = items * I::kElems;
+    const size_t want = (items + 8 * 32 * I::kRep - 1) / (8 * 32 * I::kRep);  // 8 warps per block
     size_t blocks = std::min<size_t>(want, static_cast<size_t>(sms) * 8);
-    blocks = std::max<size_t>(blocks, 1);  // the tail needs at least one block (tail < 32 elements)
+    blocks = std::max<size_t>(blocks, 1);  // the tail needs at least one block (tail < 8 elements)
     k_decode_stream<FMT><<<static_cast<unsigned>(blocks), 256, 0, st>>>(
-        static_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), units, src, dst, tail_begin, n);
+        static_cast<const typename I::In*>(src), reinterpret_cast<typename I::Out*>(dst), items, src, dst,
+        tail_begin, n);
     return cudaGetLastError();
 }
 

@@ -226,10 +226,15 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
 // in the rest, up to twelve.
 template <int BN, int FMT>
 struct PickTmem {
-    static constexpr int SB = BN <= 16 ? 16 : 8;  // B slots (2 KB or 8 KB each)
-    static constexpr int SR0 = (kSmemBudget - 1024 - SB * BN * 128) / raw_stage_bytes(FMT);
-    static constexpr int SR = SR0 > 12 ? 12 : SR0;
-    using Cfg = TmemCfg<BN, FMT, SR, SB>;
+    static constexpr int NRND = BN <= 32 ? 3 : 2;  // round slots of B tiles and TMEM A stages
+    static constexpr int ROW = raw_row_bytes(FMT);
+    static constexpr int RSK = ROW <= 64 ? 4 : ROW == 128 ? 2 : 1;
+    static constexpr int SPR = 4 / RSK;
+    static constexpr int STAGE = RSK * ROW * 128;
+    static constexpr int SR0 = (kSmemBudget - 1024 - NRND * 4 * BN * 128) / STAGE;
+    static constexpr int SR1 = SR0 > 12 ? 12 : SR0;
+    static constexpr int SR = SR1 / SPR * SPR;
+    using Cfg = TmemCfg<BN, FMT, SR, NRND>;
 };
 
 template <int BN, int FMT>
@@ -292,8 +297,8 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
         splits = r.force_splits ? r.force_splits : choose_splits(tiles_m * tiles_n, num_kb, sms);
         splits = std::max(1, std::min(splits, num_kb));
     }
-    // Each split starts on a raw-stage boundary of the fused kernel.
-    const int rk = r.kind == GemmKind::kFused ? raw_kblocks(r.a_fmt) : 1;
+    // Each split starts on a round boundary (four k-blocks) of the fused kernels.
+    const int rk = r.kind == GemmKind::kFused ? 4 : 1;
     int kb_per = (num_kb + splits - 1) / splits;
     kb_per = (kb_per + rk - 1) / rk * rk;
     splits = (num_kb + kb_per - 1) / kb_per;

@@ -189,7 +189,8 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
 }
 
 // True (warp-uniformly) if any lane's unit holds a code that the fast decode
-// path does not reproduce; those units take the scalar reference path.
+// path does not reproduce; those units take the per-code path (E4M3 subnormal
+// words flushed by mask, NaN words and BF16 NaNs by the reference rule).
 template <int FMT>
 __device__ __forceinline__ bool unit_needs_scalar(const uint4& in) {
     if constexpr (FMT == kE4M3) {
@@ -212,8 +213,8 @@ __device__ __forceinline__ void decode_store_unit(const uint4& in, uint32_t dst,
         uint32_t o[8];  // 16 values -> FP16 chunks 2col, 2col+1
         if constexpr (FMT == kE4M3) {
             if (unit_needs_scalar<kE4M3>(in)) {
-                decode_e4m3_x4_scalar(in.x, o[0], o[1]); decode_e4m3_x4_scalar(in.y, o[2], o[3]);
-                decode_e4m3_x4_scalar(in.z, o[4], o[5]); decode_e4m3_x4_scalar(in.w, o[6], o[7]);
+                decode_e4m3_x4(in.x, o[0], o[1]); decode_e4m3_x4(in.y, o[2], o[3]);
+                decode_e4m3_x4(in.z, o[4], o[5]); decode_e4m3_x4(in.w, o[6], o[7]);
             } else {
                 decode_e4m3_x4_fast(in.x, o[0], o[1]); decode_e4m3_x4_fast(in.y, o[2], o[3]);
                 decode_e4m3_x4_fast(in.z, o[4], o[5]); decode_e4m3_x4_fast(in.w, o[6], o[7]);

@@ -40,15 +40,21 @@ __device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) {
 
 // ---- E4M3 --------------------------------------------------------------------------
 
-// Bit 7 of each byte set where the E4M3 code needs the scalar path: exponent
-// field 0 with a non-zero mantissa (a subnormal, flushed by the reference) or
-// magnitude 0x7F (NaN, which the reference encodes as 0x7E00).  With
-// m = code & 0x7F (no byte carries out of its lane):
-//   m + 0x7F has bit 7 iff m >= 1;  m + 0x78 iff m >= 8;  m + 0x01 iff m == 0x7F.
+// Bit 7 of each byte set where the E4M3 code is not reproduced by the
+// hardware converter alone: exponent field 0 with a non-zero mantissa (a
+// subnormal, flushed by the reference) or magnitude 0x7F (NaN, which the
+// reference encodes as sign | 0x7E00).  With m = code & 0x7F (no byte carries
+// out of its lane): m + 0x7F has bit 7 iff m >= 1;  m + 0x78 iff m >= 8;
+// m + 0x01 iff m == 0x7F.
 __device__ __forceinline__ uint32_t e4m3_special_mask(uint32_t w) {
     const uint32_t m = w & 0x7F7F7F7Fu;
     const uint32_t ge1 = m + 0x7F7F7F7Fu, ge8 = m + 0x78787878u, nan = m + 0x01010101u;
     return ((ge1 & ~ge8) | nan) & 0x80808080u;
+}
+
+// Bit 7 of each byte set where the code is a NaN (magnitude 0x7F).
+__device__ __forceinline__ uint32_t e4m3_nan_bits(uint32_t w) {
+    return ((w & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u;
 }
 
 // Four E4M3 codes (byte 0 first) -> four FP16 values in o0, o1.  Fast path:
@@ -56,6 +62,17 @@ __device__ __forceinline__ uint32_t e4m3_special_mask(uint32_t w) {
 __device__ __forceinline__ void decode_e4m3_x4_fast(uint32_t w, uint32_t& o0, uint32_t& o1) {
     o0 = cvt_e4m3x2(static_cast<uint16_t>(w & 0xFFFFu));
     o1 = cvt_e4m3x2(static_cast<uint16_t>(w >> 16));
+}
+
+// Valid for every code but NaN (e4m3_nan_bits(w) == 0): the converter's
+// result with the codes whose exponent field is zero masked to a signed zero
+// (the converter keeps the code's sign in bit 15).  Bit 7 of each byte of
+// (w & 0x78787878) + 0x78787878 is set iff that code's exponent field is
+// non-zero; prmt replicates it over the code's FP16 lane.
+__device__ __forceinline__ void decode_e4m3_x4_flush(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    const uint32_t nz = (w & 0x78787878u) + 0x78787878u;
+    o0 = cvt_e4m3x2(static_cast<uint16_t>(w & 0xFFFFu)) & (prmt(nz, 0u, 0x9988u) | 0x80008000u);
+    o1 = cvt_e4m3x2(static_cast<uint16_t>(w >> 16)) & (prmt(nz, 0u, 0xBBAAu) | 0x80008000u);
 }
 
 // Scalar path: the reference rule code by code (valid for every code).
@@ -67,6 +84,7 @@ __device__ __forceinline__ void decode_e4m3_x4_scalar(uint32_t w, uint32_t& o0, 
 
 __device__ __forceinline__ void decode_e4m3_x4(uint32_t w, uint32_t& o0, uint32_t& o1) {
     if (e4m3_special_mask(w) == 0u) decode_e4m3_x4_fast(w, o0, o1);
+    else if (e4m3_nan_bits(w) == 0u) decode_e4m3_x4_flush(w, o0, o1);
     else decode_e4m3_x4_scalar(w, o0, o1);
 }
 
