@@ -15,8 +15,11 @@
 // latency even when it does not block, and one M = 128, K = 16 MMA occupies
 // the tensor pipe for about 40 cycles whatever BN is, so the k-block loop is
 // bounded by how many barrier operations sit on each role's path.  Per round
-// the MMA issuer waits once (rdy) and commits once (fre); each decode warp
-// waits twice (its raw stage, fre) and arrives twice (raw_empty, rdy).
+// the MMA issuer waits once (rdy) and commits once (fre).  The decode warps
+// touch no mbarrier at all: a sync warp does their waits one round ahead
+// (raw stages landed, TMEM stages freed) and their arrivals (raw stages
+// consumed, round decoded), and hands rounds to them through two pairs of
+// hardware named barriers, which cost a few tens of cycles.
 //
 // Roles (one persistent CTA per SM, same work units as gemm_kernel.cuh):
 //   warp 0      TMA producer of the raw A ring.  A raw stage holds RSK
@@ -30,25 +33,30 @@
 //               32 q + i.  Slice j = (warp - 6) / 4 of a quarter decodes
 //               k-block j of every round, whole rows of 64 values.
 //   warp 22     TMA producer of the B tiles: one per k-block of a round
+//   warp 23     sync warp of the decode warps
 // TMEM columns: [0, 2 BN) two accumulators, then from column 128 NRND round
 // slots (3, or 2 for BN = 64 where the B tiles are larger) of four A stages of
 // 32 columns (64 FP16 values of K per lane).
 //
 // Barriers, all waits bounded:
-//   raw_full / raw_empty  per raw slot: TMA bytes / one arrival from each of
-//                         the 4 x RSK decode warps that read the slot.  SR is a
-//                         multiple of SPR, so a slot always holds the same
-//                         stage position of a round and is read by the same
-//                         warps, which wait on every fill of it.
-//   rdy[r % NRND]         round r is ready: one arrival from each of the 16
-//                         decode warps (after tcgen05.st has completed) and the
-//                         B producer's arrival with the round's B bytes.
+//   raw_full / raw_empty  per raw slot: TMA bytes / the sync warp's arrival
+//                         once the decode warps have read the stage.
+//   rdy[r % NRND]         round r is ready: the sync warp's arrival (the decode
+//                         warps' tcgen05.st has completed) and the B
+//                         producer's arrival with the round's B bytes.
 //   fre[r % NRND]         round r's MMAs have completed (one commit): its TMEM
 //                         stages and B tiles may be overwritten.
 //   acc_full / acc_empty  as in gemm_kernel.cuh.
+//   named START[r % 2]    the sync warp arrives once round r's raw stages have
+//                         landed and its TMEM stages are free; the 16 decode
+//                         warps wait.
+//   named DONE[r % 2]     the decode warps arrive once round r is in TMEM and
+//                         its raw words are consumed; the sync warp waits.
 // Every role takes part in every round, including the short last round of a
 // unit, so each waiter has seen the previous phase of every barrier it waits
-// on and a parity wait cannot pass on a stale phase.
+// on and a parity wait cannot pass on a stale phase.  The named barriers have
+// no timeout, so the sync warp and the decode warps go through all of them
+// for every round even after an abort (they then skip the waits and the work).
 #pragma once
 
 #include "gemm_kernel.cuh"
@@ -69,11 +77,25 @@ struct TmemCfg {
     static constexpr int NBOX = RSK * ROW_BYTES / 128;    // 128-byte boxes per stage
     static constexpr int STAGE_BYTES = NBOX * 16384;
     static constexpr int SR = SR_;                        // raw ring slots
+    // Raw stages the producer keeps in flight (about 96 KB): a CTA that asks
+    // for its whole ring at once gets all stages at about the same time, late,
+    // because HBM serves the requests of all CTAs interleaved; a bounded
+    // number in flight lands in order and the first round arrives early.
+    // The stage waited for must not have been refilled yet: INFLIGHT < SR.
+    static constexpr int INFLIGHT0 = (96 * 1024) / STAGE_BYTES < 1 ? 1 : (96 * 1024) / STAGE_BYTES;
+    static constexpr int INFLIGHT = INFLIGHT0 < SR - 1 ? INFLIGHT0 : SR - 1;
     static constexpr int NRND = NRND_;                    // round slots (TMEM A stages, B tiles)
     static constexpr int B_BYTES = BN * 128;              // one k-block of B
     static constexpr int DECODE_WARP0 = 6;
     static constexpr int B_WARP = DECODE_WARP0 + ND;
-    static constexpr int NUM_THREADS = (B_WARP + 1) * 32;
+    static constexpr int SYNC_WARP = B_WARP + 1;
+    static constexpr int NUM_THREADS = (SYNC_WARP + 1) * 32;
+    // The sync warp hands whole rounds to the decode warps when the raw ring
+    // holds at least two rounds (all formats but TF32, whose 128 KB rounds
+    // do not fit twice); otherwise each decode warp waits and arrives itself.
+    static constexpr bool SYNCW = SR >= 2 * SPR;
+    // Named barriers (0 is __syncthreads): START 1-2, DONE 3-4.
+    static constexpr uint32_t NB_START = 1, NB_DONE = 3, NB_COUNT = (ND + 1) * 32;
 
     static constexpr int A_COL0 = 128;
     static constexpr int TMEM_COLS = 512;
@@ -181,6 +203,53 @@ __device__ __forceinline__ uint32_t unit_special_mask(const uint4& in) {
         return 0u;
 }
 
+// One work unit of the narrow kernel: tile (tm, tn), split sp, k-blocks
+// [kb0, kb1).
+struct NUnit {
+    int tm, tn, sp, kb0, kb1;
+};
+
+// This CTA's work units (persistent: blockIdx.x, + gridDim.x, ...), in the
+// same order for every role.
+struct NCursor {
+    int u;
+};
+
+__device__ __forceinline__ void ncur_init(const GemmArgs&, NCursor& c) { c.u = blockIdx.x; }
+
+__device__ __forceinline__ bool ncur_next(const GemmArgs& p, NCursor& c, NUnit& x) {
+    if (c.u >= p.num_units) return false;
+    unit_coords(p, c.u, x.tm, x.tn, x.sp);
+    unit_kblocks(p, x.sp, x.kb0, x.kb1);
+    c.u += gridDim.x;
+    return true;
+}
+
+// Decode k-block `sub` of the raw stage at `raw` for tile row `row` (this
+// thread's TMEM lane) and store its 64 FP16 values into TMEM columns
+// [ta, ta + 32).  The stores are asynchronous (tcgen05.wait::st).
+template <class C>
+__device__ __forceinline__ void decode_kblock(uint32_t raw, int sub, int row, uint32_t ta) {
+#pragma unroll
+    for (int h = 0; h < C::H; ++h) {
+        uint4 in[C::UPH];
+#pragma unroll
+        for (int x = 0; x < C::UPH; ++x) in[x] = lds128(tmem_raw_addr<C>(raw, sub, row, h * C::UPH + x));
+        bool scalar = false;
+        if constexpr (C::FMT == kE4M3 || C::FMT == kBF16 || C::FMT == kTF32) {
+            uint32_t m = 0;
+#pragma unroll
+            for (int x = 0; x < C::UPH; ++x) m |= unit_special_mask<C::FMT>(in[x]);
+            scalar = __any_sync(0xFFFFFFFFu, m != 0u);
+        }
+        uint32_t o[C::WPH];
+#pragma unroll
+        for (int x = 0; x < C::UPH; ++x) decode_unit_words<C::FMT>(in[x], o + x * C::WPU, scalar);
+        if constexpr (C::WPH == 32) tmem_st_32x32b_x32(ta, *reinterpret_cast<const uint32_t(*)[32]>(o));
+        else tmem_st_32x32b_x16(ta + h * 16, *reinterpret_cast<const uint32_t(*)[16]>(o));
+    }
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     k_fused_tmem(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs p) {
@@ -206,10 +275,10 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::SR; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], 4 * C::RSK);
+            mbar_init(&raw_empty[s], C::SYNCW ? 1 : 4 * C::RSK);
         }
         for (int s = 0; s < C::NRND; ++s) {
-            mbar_init(&rdy[s], C::ND + 1);
+            mbar_init(&rdy[s], C::SYNCW ? 2 : C::ND + 1);
             mbar_init(&fre[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -235,10 +304,11 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         // ---------------- TMA producer: raw A stages ----------------
         uint32_t st = 0;  // CTA-wide stage number
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-            int tm, tn, sp, kb0, kb1;
-            unit_coords(p, u, tm, tn, sp);
-            unit_kblocks(p, sp, kb0, kb1);
+        NCursor cur;
+        ncur_init(p, cur);
+        NUnit x;
+        while (ok && ncur_next(p, cur, x)) {
+            const int tm = x.tm, kb0 = x.kb0, kb1 = x.kb1;
             for (int kb = kb0; ok && kb < kb1; kb += C::DK) {
 #pragma unroll 1
                 for (int pos = 0; pos < C::SPR; ++pos, ++st) {
@@ -246,6 +316,15 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                     if (!__all_sync(0xFFFFFFFFu, mbar_wait(&raw_empty[rs], (fill & 1u) ^ 1u, abort_flag))) {
                         ok = false;
                         break;
+                    }
+                    if (C::INFLIGHT > 0 && st >= static_cast<uint32_t>(C::INFLIGHT)) {
+                        // This warp issued every earlier stage and waits for each
+                        // of them in order, so the parity cannot be stale.
+                        const uint32_t old = st - C::INFLIGHT;
+                        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&raw_full[old % C::SR], (old / C::SR) & 1u, abort_flag))) {
+                            ok = false;
+                            break;
+                        }
                     }
                     if (elect_one()) {
                         mbar_arrive_expect_tx(&raw_full[rs], C::STAGE_BYTES);
@@ -265,10 +344,11 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         // ---------------- TMA producer: the four B tiles of each round ----------------
         uint32_t r = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-            int tm, tn, sp, kb0, kb1;
-            unit_coords(p, u, tm, tn, sp);
-            unit_kblocks(p, sp, kb0, kb1);
+        NCursor cur;
+        ncur_init(p, cur);
+        NUnit x;
+        while (ok && ncur_next(p, cur, x)) {
+            const int tn = x.tn, kb0 = x.kb0, kb1 = x.kb1;
             for (int kb = kb0; kb < kb1; kb += C::DK, ++r) {
                 const int cnt = min(C::DK, kb1 - kb);
                 const uint32_t slot = r % C::NRND, use = r / C::NRND;
@@ -288,10 +368,11 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         uint32_t r = 0;
         int t = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x, ++t) {
-            int tm, tn, sp, kb0, kb1;
-            unit_coords(p, u, tm, tn, sp);
-            unit_kblocks(p, sp, kb0, kb1);
+        NCursor cur;
+        ncur_init(p, cur);
+        NUnit x;
+        for (; ok && ncur_next(p, cur, x); ++t) {
+            const int kb0 = x.kb0, kb1 = x.kb1;
             const int acc = t & 1;
             const uint32_t aph = (t >> 1) & 1;
             if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag))) { ok = false; break; }
@@ -333,15 +414,17 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         // ---------------- epilogue ----------------
         const int quarter = warp & 3;
         int t = 0;
-        for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++t) {
-            int tm, tn, sp;
-            unit_coords(p, u, tm, tn, sp);
+        NCursor cur;
+        ncur_init(p, cur);
+        NUnit x;
+        for (; ncur_next(p, cur, x); ++t) {
             const int acc = t & 1;
             const uint32_t aph = (t >> 1) & 1;
             const bool ok = mbar_wait(&acc_full[acc], aph, abort_flag);
             if (!__all_sync(0xFFFFFFFFu, ok)) break;
             tc_fence_after();
-            const int row = tm * C::BM + quarter * 32 + lane;
+            const int trow = quarter * 32 + lane;
+            const int row = x.tm * C::BM + trow;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * C::BN);
 #pragma unroll 1
@@ -349,10 +432,55 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                 uint32_t v[C::CW];
                 tmem_ld_chunk<C::CW>(t_row + c, v);
                 tmem_wait_ld();
-                store_row_chunk<C::CW>(p, sp, row, tn * C::BN + c, v);
+                store_row_chunk<C::CW>(p, x.sp, row, x.tn * C::BN + c, v);
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
+        }
+    } else if (warp == C::SYNC_WARP) {
+        // ---------------- sync warp: the decode warps' mbarrier traffic, one round ahead ----------------
+        if constexpr (C::SYNCW) {
+            uint32_t nr = 0;  // rounds of this CTA
+            {
+                NCursor cur;
+                ncur_init(p, cur);
+                NUnit x;
+                while (ncur_next(p, cur, x)) nr += static_cast<uint32_t>((x.kb1 - x.kb0 + C::DK - 1) / C::DK);
+            }
+            bool ok = true;
+            // Round r's raw stages have landed and its TMEM stages are free.
+            auto ready = [&](uint32_t r) -> bool {
+                bool good = true;
+#pragma unroll 1
+                for (int pos = 0; pos < C::SPR && good; ++pos) {
+                    const uint32_t st = r * C::SPR + pos;
+                    good = __all_sync(0xFFFFFFFFu, mbar_wait(&raw_full[st % C::SR], (st / C::SR) & 1u, abort_flag));
+                }
+                const uint32_t use = r / C::NRND;
+                return good && __all_sync(0xFFFFFFFFu, mbar_wait(&fre[r % C::NRND], (use & 1u) ^ 1u, abort_flag));
+            };
+            if (nr > 0) {
+                ok = ready(0);
+                named_bar_arrive(C::NB_START, C::NB_COUNT);
+            }
+            for (uint32_t r = 0; r < nr; ++r) {
+                // Open round r + 1 as soon as it is ready, so a decode warp that
+                // finishes round r early goes on without waiting for the others.
+                // START[(r + 1) % 2] last served round r - 1, which every decode
+                // warp passed before the DONE of round r - 1 that this warp has
+                // already waited for.
+                if (r + 1 < nr) {
+                    if (ok) ok = ready(r + 1);
+                    named_bar_arrive(C::NB_START + ((r + 1) & 1u), C::NB_COUNT);
+                }
+                named_bar_sync(C::NB_DONE + (r & 1u), C::NB_COUNT);
+                if (ok && lane == 0) {
+#pragma unroll 1
+                    for (int pos = 0; pos < C::SPR; ++pos) mbar_arrive(&raw_empty[(r * C::SPR + pos) % C::SR]);
+                    mbar_arrive(&rdy[r % C::NRND]);
+                }
+                __syncwarp();
+            }
         }
     } else if (warp < C::B_WARP) {
         // ---------------- decode warps: k-block j of each round -> FP16 words -> TMEM ----------------
@@ -363,53 +491,56 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                 static_cast<uint32_t>(C::A_COL0 + j * 32);
         uint32_t r = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-            int tm, tn, sp, kb0, kb1;
-            unit_coords(p, u, tm, tn, sp);
-            unit_kblocks(p, sp, kb0, kb1);
-            for (int kb = kb0; kb < kb1; kb += C::DK, ++r) {
-                const bool mine = j < kb1 - kb;  // the short last round of a unit
-                const uint32_t st = r * C::SPR + pos;
-                const uint32_t rs = st % C::SR, fill = st / C::SR;
-                const uint32_t slot = r % C::NRND, use = r / C::NRND;
-                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&raw_full[rs], fill & 1u, abort_flag))) { ok = false; break; }
-                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&fre[slot], (use & 1u) ^ 1u, abort_flag))) { ok = false; break; }
-                tc_fence_after();
-                if (mine) {
-                    const uint32_t raw = sbase + C::OFF_R + rs * C::STAGE_BYTES;
-                    const uint32_t ta = t_lane + static_cast<uint32_t>(slot * C::DK * 32);
-#pragma unroll
-                    for (int h = 0; h < C::H; ++h) {
-                        uint4 in[C::UPH];
-#pragma unroll
-                        for (int x = 0; x < C::UPH; ++x)
-                            in[x] = lds128(tmem_raw_addr<C>(raw, sub, row, h * C::UPH + x));
-                        bool scalar = false;
-                        if constexpr (C::FMT == kE4M3 || C::FMT == kBF16 || C::FMT == kTF32) {
-                            uint32_t m = 0;
-#pragma unroll
-                            for (int x = 0; x < C::UPH; ++x) m |= unit_special_mask<C::FMT>(in[x]);
-                            scalar = __any_sync(0xFFFFFFFFu, m != 0u);
-                        }
-                        uint32_t o[C::WPH];
-#pragma unroll
-                        for (int x = 0; x < C::UPH; ++x) decode_unit_words<C::FMT>(in[x], o + x * C::WPU, scalar);
-                        if constexpr (C::WPH == 32) tmem_st_32x32b_x32(ta, *reinterpret_cast<const uint32_t(*)[32]>(o));
-                        else tmem_st_32x32b_x16(ta + h * 16, *reinterpret_cast<const uint32_t(*)[16]>(o));
+        if constexpr (C::SYNCW) {
+            NCursor cur;
+            ncur_init(p, cur);
+            NUnit x;
+            while (ncur_next(p, cur, x)) {
+                const int kb0 = x.kb0, kb1 = x.kb1;
+                for (int kb = kb0; kb < kb1; kb += C::DK, ++r) {
+                    named_bar_sync(C::NB_START + (r & 1u), C::NB_COUNT);
+                    // The short last round of a unit; nothing after an abort.
+                    const bool mine = j < kb1 - kb && *abort_flag == 0;
+                    tc_fence_after();
+                    if (mine) {
+                        const uint32_t st = r * C::SPR + pos;
+                        decode_kblock<C>(sbase + C::OFF_R + (st % C::SR) * C::STAGE_BYTES, sub, row,
+                                         t_lane + static_cast<uint32_t>((r % C::NRND) * C::DK * 32));
+                        tmem_wait_st();
                     }
+                    tc_fence_before();
+                    named_bar_arrive(C::NB_DONE + (r & 1u), C::NB_COUNT);
                 }
-                // The raw words are consumed (decoded above): release the stage.
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&raw_empty[rs]);
-                if (mine) tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&rdy[slot]);
+            }
+        } else {
+            bool ok = true;
+            NCursor cur;
+            ncur_init(p, cur);
+            NUnit x;
+            while (ok && ncur_next(p, cur, x)) {
+                const int kb0 = x.kb0, kb1 = x.kb1;
+                for (int kb = kb0; kb < kb1; kb += C::DK, ++r) {
+                    const bool mine = j < kb1 - kb;  // the short last round of a unit
+                    const uint32_t st = r * C::SPR + pos;
+                    const uint32_t rs = st % C::SR, fill = st / C::SR;
+                    const uint32_t slot = r % C::NRND, use = r / C::NRND;
+                    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&raw_full[rs], fill & 1u, abort_flag))) { ok = false; break; }
+                    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&fre[slot], (use & 1u) ^ 1u, abort_flag))) { ok = false; break; }
+                    tc_fence_after();
+                    if (mine)
+                        decode_kblock<C>(sbase + C::OFF_R + rs * C::STAGE_BYTES, sub, row,
+                                         t_lane + static_cast<uint32_t>(slot * C::DK * 32));
+                    // The raw words are consumed (decoded above): release the stage.
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                    if (mine) tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&rdy[slot]);
+                }
             }
         }
     }
-
     __syncwarp();
     tc_fence_before();
     __syncthreads();

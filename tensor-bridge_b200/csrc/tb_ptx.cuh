@@ -111,6 +111,20 @@ __device__ __forceinline__ bool elect_one() {
     return pred != 0;
 }
 
+// ---- named (hardware) CTA barriers ---------------------------------------------------
+
+// Wait at named barrier `id` until `count` threads (a multiple of 32, whole
+// warps) have arrived or waited on it.  Unlike an mbarrier wait this cannot
+// time out: every participant must reach it the same number of times.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Arrive at named barrier `id` without waiting.
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---- proxy fences ---------------------------------------------------------------
 
 // Order this thread's generic-proxy shared-memory writes before later
