@@ -395,36 +395,50 @@ def weights_q(torch, tb, fmt, rows: int, cols: int, std: float, seed: int):
     return q, float(np.float32(1.0) / np.float32(scale))
 
 
-def time_rotating(torch, fns, iters: int) -> float:
-    """Median device time (ms) per launch of a back-to-back sequence: each
-    iteration launches every callable of `fns` once, in order, between one
-    CUDA-event pair, and the time is divided by len(fns).  The callables work
-    on distinct buffers whose total is larger than the 126 MB L2, so every
-    launch reads its inputs from HBM, as consecutive layers of a model do; no
-    per-launch event or host gap is inside the figure."""
+def time_graph(torch, fns, iters: int = 20) -> float:
+    """Median device time (ms) per launch of a back-to-back sequence: every
+    callable of `fns` once, in order, captured in one CUDA graph that is
+    replayed `iters` times, each replay between a CUDA-event pair, divided by
+    len(fns).  The callables work on distinct buffers whose total is larger
+    than the 126 MB L2, so every launch reads its inputs from HBM, as
+    consecutive layers of a model do."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for fn in fns:  # first calls (kernel attributes) outside the capture
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for fn in fns:
+            fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
-    for fn in fns:
-        fn()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
     for a, b in ev:
         a.record(stream)
-        for fn in fns:
-            fn()
+        g.replay()
         b.record(stream)
     torch.cuda.synchronize()
-    return statistics.median(a.elapsed_time(b) for a, b in ev) / len(fns)
+    ms = statistics.median(a.elapsed_time(b) for a, b in ev) / len(fns)
+    del g
+    return ms
 
 
 ROTATE_BYTES = 400_000_000  # > 3 x L2
 
 
-def mlp_weight_only(torch, tb, peaks, iters: int = 10):
+def mlp_weight_only(torch, tb, peaks, iters: int = 20):
     """Weight-only inference shapes: W 14336 x 4096 and 4096 x 14336 (output
     features x K) in E4M3 and packed E2M1, activations FP16 [tokens x K],
     FP32 out, tokens 1/16/128/2048.  Fused decode-in-shared-memory GEMM
     against decode kernel + GEMM.  Each figure is per launch of a back-to-back
     sequence over C copies of the weight (C x stored bytes > 400 MB, so every
-    launch streams its weight from HBM).  Algorithmic bytes = stored W + X + D."""
+    launch streams its weight from HBM) inside a CUDA graph, median of 20
+    replays.  Algorithmic bytes = stored W + X + D."""
     out = []
     for (M, K) in ((14336, 4096), (4096, 14336)):
         for fname, fmt in (("e4m3", tb.Format.E4M3), ("e2m1", tb.Format.E2M1)):
@@ -439,12 +453,12 @@ def mlp_weight_only(torch, tb, peaks, iters: int = 10):
                 D = torch.empty(M, N, dtype=torch.float32, device="cuda")
                 wsb = tb.fused_workspace_bytes(fmt, M, N, K)
                 ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda")
-                fused = time_rotating(torch, [lambda Ai=Ai: tb.gemm_fused(fmt, Ai, B, D, M, N, K, alpha=alpha,
+                fused = time_graph(torch, [lambda Ai=Ai: tb.gemm_fused(fmt, Ai, B, D, M, N, K, alpha=alpha,
                                                                           workspace=ws, workspace_bytes=wsb)
                                               for Ai in As], iters)
-                dec = time_rotating(torch, [lambda i=i, Ai=Ai: tb.decode(fmt, Ai, A16[i & 1], M * K)
+                dec = time_graph(torch, [lambda i=i, Ai=Ai: tb.decode(fmt, Ai, A16[i & 1], M * K)
                                             for i, Ai in enumerate(As)], iters)
-                gemm = time_rotating(torch, [lambda i=i: tb.gemm_f16(A16[i & 1], B, D, M, N, K, alpha=alpha)
+                gemm = time_graph(torch, [lambda i=i: tb.gemm_f16(A16[i & 1], B, D, M, N, K, alpha=alpha)
                                              for i in range(copies)], iters)
                 nbytes = A.numel() + N * K * 2 + M * N * 4
                 flops = 2.0 * M * N * K
@@ -457,11 +471,11 @@ def mlp_weight_only(torch, tb, peaks, iters: int = 10):
     return out
 
 
-def decode_streams(torch, tb, peaks, rows: int = 14336, cols: int = 4096, iters: int = 10):
+def decode_streams(torch, tb, peaks, rows: int = 14336, cols: int = 4096, iters: int = 20):
     """The standalone decode streamers on a 14336 x 4096 weight per format
     (N(0, 0.02) quantized per tensor): per launch of a back-to-back sequence
     alternating over two (input, output) pairs, 2 x (stored + FP16) bytes >
-    L2.  Algorithmic bytes = stored bytes read + FP16 bytes written."""
+    L2, inside a CUDA graph, median of 20 replays.  Algorithmic bytes = stored bytes read + FP16 bytes written."""
     n = rows * cols
     out = {}
     F = tb.Format
@@ -477,7 +491,7 @@ def decode_streams(torch, tb, peaks, rows: int = 14336, cols: int = 4096, iters:
             del a
         pairs = [(A, torch.empty(n, dtype=torch.float16, device="cuda")),
                  (A.clone(), torch.empty(n, dtype=torch.float16, device="cuda"))]
-        ms = time_rotating(torch, [lambda s=s, d=d: tb.decode(fmt, s, d, n) for s, d in pairs] * 2, iters)
+        ms = time_graph(torch, [lambda s=s, d=d: tb.decode(fmt, s, d, n) for s, d in pairs] * 2, iters)
         nbytes = A.numel() + 2 * n
         out[name] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
                      "pct_hbm": 100 * nbytes / ms / 1e6 / peaks["hbm_gbs"]}

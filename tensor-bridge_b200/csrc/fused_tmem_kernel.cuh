@@ -1,4 +1,4 @@
-// fused_tmem_kernel.cuh -- fused decode + GEMM for narrow tiles (BN <= 64),
+// fused_tmem_kernel.cuh -- fused decode + GEMM for narrow tiles (BN <= 128),
 // with the decoded weights written to tensor memory instead of shared memory.
 //
 //   D[M x N] = alpha * decode(A)[M x K] * B[N x K]^T
@@ -34,9 +34,10 @@
 //               k-block j of every round, whole rows of 64 values.
 //   warp 22     TMA producer of the B tiles: one per k-block of a round
 //   warp 23     sync warp of the decode warps
-// TMEM columns: [0, 2 BN) two accumulators, then from column 128 NRND round
-// slots (3, or 2 for BN = 64 where the B tiles are larger) of four A stages of
-// 32 columns (64 FP16 values of K per lane).
+// TMEM columns: [0, 2 BN) two accumulators, then from column max(128, 2 BN)
+// NRND round slots (3 for BN <= 32; 2 for BN = 64, where the B tiles are
+// larger, and for BN = 128, where TMEM holds no more) of four A stages of 32
+// columns (64 FP16 values of K per lane).
 //
 // Barriers, all waits bounded:
 //   raw_full / raw_empty  per raw slot: TMA bytes / the sync warp's arrival
@@ -97,7 +98,7 @@ struct TmemCfg {
     // Named barriers (0 is __syncthreads): START 1-2, DONE 3-4.
     static constexpr uint32_t NB_START = 1, NB_DONE = 3, NB_COUNT = (ND + 1) * 32;
 
-    static constexpr int A_COL0 = 128;
+    static constexpr int A_COL0 = 2 * BN > 128 ? 2 * BN : 128;
     static constexpr int TMEM_COLS = 512;
     static constexpr int CW = BN < 32 ? BN : 32;
 
@@ -118,7 +119,7 @@ struct TmemCfg {
 
     static constexpr uint32_t IDESC = idesc_make(0u, 0u, BM, BN);
 
-    static_assert(BN == 16 || BN == 32 || BN == 64, "narrow tiles only");
+    static_assert(BN == 16 || BN == 32 || BN == 64 || BN == 128, "narrow tiles only");
     static_assert(RSK * SPR == DK && NBOX >= 1 && RSK * ROW_BYTES == NBOX * 128, "raw stage geometry");
     static_assert(WPH == 32 || WPH == 16, "TMEM store width");
     static_assert(2 * BN <= A_COL0 && A_COL0 + NRND * DK * 32 <= TMEM_COLS && NRND >= 2, "TMEM budget");

@@ -275,6 +275,10 @@ static cudaError_t run_bn(int bn, const GemmRequest& r, const GemmArgs& a, cudaS
     if constexpr (MODE == kModeDecode) {
         if (bn == 16) return run_tmem<16, FMT>(r, a, st, dev, why);
         if (bn == 64) return run_tmem<64, FMT>(r, a, st, dev, why);
+        // 128 columns: the B tiles (64 KB a round) leave room for a raw ring of
+        // two rounds only with the one-byte and half-byte formats.
+        if constexpr (raw_row_bytes(FMT) <= 64)
+            if (bn == 128) return run_tmem<128, FMT>(r, a, st, dev, why);
     }
     switch (bn) {
         case 16: return run<16, MODE, FMT>(r, a, st, dev, why);

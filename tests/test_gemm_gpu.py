@@ -69,6 +69,8 @@ SHAPES = [
     (1000, 64, 1536),
     (300, 24, 4160),     # ragged M, K with a partial raw stage
     (256, 8, 80),
+    (300, 100, 1056),    # 65..128 tokens (128-column narrow tiles), partial last round
+    (1000, 128, 4160),
 ]
 
 
