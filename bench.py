@@ -683,6 +683,32 @@ def traffic_from_profiles(label: str):
     return None
 
 
+def profile_case(case: str):
+    """Five launches of one fused weight-only GEMM: A = N(0, 0.02) weights of
+    the given format (per-tensor scale), B = N(0, 1) FP16 activations."""
+    import torch
+    tb = load_package()
+    fname, shape = case.split(":")
+    M, N, K = (int(v) for v in shape.lower().split("x"))
+    fmt = {"e4m3": tb.Format.E4M3, "e2m1": tb.Format.E2M1, "bf16": tb.Format.BF16, "tf32": tb.Format.TF32}[fname]
+    if fname in FORMAT_MAX:
+        A, alpha = weights_q(torch, tb, fmt, M, K, 0.02, seed=1)
+    else:
+        a = torch.randn(M, K, device="cuda") * 0.02
+        A = torch.empty(tb.stored_bytes(fmt, M * K), dtype=torch.uint8, device="cuda")
+        tb.quantize(fmt, a, A, M * K)
+        alpha = 1.0
+    B = torch.randn(N, K, device="cuda").half()
+    D = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    wsb = tb.fused_workspace_bytes(fmt, M, N, K)
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda")
+    for _ in range(5):
+        tb.gemm_fused(fmt, A, B, D, M, N, K, alpha=alpha, workspace=ws, workspace_bytes=wsb)
+    torch.cuda.synchronize()
+    assert tb.device_error() == 0, "a kernel reported a device-side wait timeout"
+    print(json.dumps({"profile_case": case, "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -692,7 +718,13 @@ def main():
     ap.add_argument("--size", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the MLP-shape and 8192^3 FP4 sub-objects")
+    ap.add_argument("--profile-case", metavar="FMT:MxNxK",
+                    help="run only 5 fused weight-only GEMMs of this case (e.g. e4m3:14336x16x4096) and exit; "
+                         "the command profiles/ captures of single kernels use")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         reference_arm(args)
