@@ -499,6 +499,29 @@ def decode_streams(torch, tb, peaks, rows: int = 14336, cols: int = 4096, iters:
     return out
 
 
+def int8_square(torch, tb, n: int = 4096, iters: int = 10):
+    """The INT8 path at n^3: INT8 GEMM on tcgen05 kind::i8 (exact INT32), and
+    the reference-shaped FP8 -> INT8 fused entry (both operands converted with
+    scale 127/448, then the GEMM).  Dense integer peak 4.5 POPS."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(8)
+    A8 = torch.randint(-128, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    B8 = torch.randint(-128, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    D = torch.empty(n, n, dtype=torch.int32, device="cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    ms = time_each(torch, lambda: tb.gemm_i8(A8, B8, D, n, n, n), iters, flush)
+    A, _ = weights_q(torch, tb, tb.Format.E4M3, n, n, 1.0, seed=9)
+    B, _ = weights_q(torch, tb, tb.Format.E4M3, n, n, 1.0, seed=10)
+    wsb = tb.lib().tb_gemm_fp8_fused_int8_workspace(n, n, n)
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    scale = float(np.float32(127.0) / np.float32(448.0))
+    ms_f = time_each(torch, lambda: tb.gemm_fp8_fused_int8(A, B, D, n, n, n, scale, ws, wsb), iters, flush)
+    ops = 2.0 * n ** 3
+    return {"M": n, "N": n, "K": n, "gemm_i8_ms": ms, "gemm_i8_tops": ops / ms / 1e9,
+            "pct_i8_dense_peak": 100 * ops / ms / 1e9 / 4500.0, "fp8_fused_int8_ms": ms_f,
+            "fp8_fused_int8_tops": ops / ms_f / 1e9}
+
+
 def fp4_square(torch, tb, peaks, n: int = 8192, iters: int = 10):
     """Large square fused GEMM: A packed E2M1 from N(0, 1) with scale 6/maxabs,
     B FP16 N(0, 1), FP32 accumulation, FP16 output."""
@@ -806,6 +829,7 @@ def main():
         line["decode_stream_14336x4096"] = decode_streams(torch, tb, peaks)
         line["weight_only_mlp"] = mlp_weight_only(torch, tb, peaks)
         line["fp4_8192_fused"] = fp4_square(torch, tb, peaks)
+        line["int8_4096"] = int8_square(torch, tb)
         line["sharded_weight_gemm"] = sharded_weight_gemm(torch, tb, dist)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline((M, N, K))

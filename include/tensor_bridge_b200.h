@@ -204,6 +204,42 @@ tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, i
                                  void* workspace, size_t workspace_bytes, tb_stream_t stream);
 size_t tb_gemm_fp8_fused_workspace(int M, int N, int K);
 
+/* ---- INT8 path (the reference's integer tensor-core path) ----------------
+ *
+ * E4M3 -> INT8 as src/gemm.cu:35-41 converts:
+ * (int8_t)__float2int_rn(__half2float(fp8_e4m3_to_half(c)) * scale) -- the
+ * reference decode to FP16, an FP32 product with the per-tensor scale (127 /
+ * maxabs keeps every value in [-127, 127]), round to nearest even into an
+ * int32 (clamped to the int32 range, NaN -> 0) and the low byte of that, so
+ * out-of-range products wrap exactly as the reference's cast does. */
+
+/* n codes, straight (decode_fp8_to_int8's A operand). */
+tb_status tb_decode_e4m3_to_i8(const uint8_t* src, int8_t* dst, size_t n, float scale, tb_stream_t stream);
+
+/* src [rows x cols] -> dst [cols x rows]: B8[col * K + k] of
+ * decode_fp8_to_int8 (src/gemm.cu:39) with rows = K, cols = N. */
+tb_status tb_decode_e4m3_to_i8_transposed(const uint8_t* src, int8_t* dst, int rows, int cols, float scale,
+                                          tb_stream_t stream);
+
+/* Mirror of decode_fp8_to_int8 (src/gemm.cu:35-41): A [M x K] straight into
+ * A8, B [K x N] transposed into B8 [N x K]; either pair may be NULL. */
+tb_status tb_decode_fp8_to_int8(const uint8_t* A, const uint8_t* B, int8_t* A8, int8_t* B8, int M, int N, int K,
+                                float scale, tb_stream_t stream);
+
+/* Replaces gemm_int8_wmma (src/gemm.cu:58-70): D [M x N] INT32 = A8 [M x K]
+ * INT8 * B8^T, B8 [N x K] INT8 (the reference's column-major B), exact int32
+ * accumulation on tcgen05.mma kind::i8.  K a multiple of 16, A and B 16-byte
+ * aligned.  Any M, N (the reference needs multiples of 16). */
+tb_status tb_gemm_i8(const int8_t* A, const int8_t* B, int32_t* D, int M, int N, int K, tb_stream_t stream);
+
+/* Mirror of gemm_fp8_fused_int8 (src/gemm_fused.cu:52-81): A [M x K] and
+ * B [K x N] E4M3, both converted to INT8 with `scale` as above, D [M x N]
+ * INT32.  The converted operands go to `workspace`
+ * (tb_gemm_fp8_fused_int8_workspace bytes), then the kind::i8 GEMM runs. */
+tb_status tb_gemm_fp8_fused_int8(const uint8_t* A, const uint8_t* B, int32_t* D, int M, int N, int K, float scale,
+                                 void* workspace, size_t workspace_bytes, tb_stream_t stream);
+size_t tb_gemm_fp8_fused_int8_workspace(int M, int N, int K);
+
 /* ---- column-sharded weight GEMM over NCCL -------------------------------- */
 /* The reference is single-GPU; this is the B200 addition for weights too large
  * or slow for one GPU.  The weight's M rows (output features) are split into

@@ -41,6 +41,8 @@ def lib():
         l.oracle_gemm.argtypes = [i, p, i, p, p, i, i, i, i, i, f, i, i]
         l.oracle_f32_to_f16.restype = ctypes.c_uint16
         l.oracle_f32_to_f16.argtypes = [f]
+        l.oracle_decode_e4m3_i8.argtypes = [p, p, sz, f]
+        l.oracle_gemm_i8.argtypes = [p, p, p, i, i, i, i]
         _lib = l
     return _lib
 
@@ -150,3 +152,20 @@ def per_tensor_scale(x: np.ndarray, fmt: int) -> float:
         return 1.0
     m = float(np.max(np.abs(x))) if x.size else 0.0
     return float(np.float32(FORMAT_MAX[fmt]) / np.float32(m if m > 0 else 1.0))
+
+
+def decode_e4m3_i8(codes: np.ndarray, scale: float) -> np.ndarray:
+    """E4M3 codes -> INT8 by the reference's integer-path rule (src/gemm.cu:35-41)."""
+    src = np.ascontiguousarray(np.asarray(codes, dtype=np.uint8).ravel())
+    out = np.empty(src.size, dtype=np.int8)
+    lib().oracle_decode_e4m3_i8(src.ctypes.data, out.ctypes.data, src.size, float(scale))
+    return out
+
+
+def gemm_i8(A8: np.ndarray, B8: np.ndarray, M: int, N: int, K: int, threads: int = 0) -> np.ndarray:
+    """D [M x N] INT32 = A8 [M x K] * B8 [N x K]^T (src/gemm.cu:58-70)."""
+    a = np.ascontiguousarray(np.asarray(A8, dtype=np.int8).ravel())
+    b = np.ascontiguousarray(np.asarray(B8, dtype=np.int8).ravel())
+    out = np.empty(M * N, dtype=np.int32)
+    lib().oracle_gemm_i8(a.ctypes.data, b.ctypes.data, out.ctypes.data, M, N, K, threads)
+    return out.reshape(M, N)

@@ -301,3 +301,44 @@ void oracle_gemm(int a_fmt, const void* A, int b_fmt, const void* B, void* D, in
     }
     free(bf);
 }
+
+/* ---- INT8 path -------------------------------------------------------------------------- */
+
+/* decode_fp8_to_int8, src/gemm.cu:35-41, per element:
+ * (int8_t)__float2int_rn(__half2float(fp8_e4m3_to_half(c)) * scale).  The FP16
+ * decode is the reference primitive (fp8.h:23-31) and widens exactly; the
+ * product is one FP32 multiply; __float2int_rn rounds to nearest even and the
+ * conversion it compiles to (cvt.rni.s32.f32) clamps to the int32 range and
+ * gives 0 for NaN; the int8_t cast keeps the low byte. */
+int8_t oracle_e4m3_to_i8(uint8_t c, float scale) {
+    const float v = oracle_f16_to_f32(oracle_e4m3_to_f16(c)) * scale;
+    int32_t r;
+    if (v != v) r = 0;
+    else if (v >= 2147483648.0f) r = INT32_MAX;
+    else if (v <= -2147483648.0f) r = INT32_MIN;
+    else r = (int32_t)nearbyintf(v); /* default rounding: nearest, ties to even */
+    return (int8_t)(uint8_t)((uint32_t)r & 0xFFu);
+}
+
+void oracle_decode_e4m3_i8(const uint8_t* src, int8_t* dst, size_t n, float scale) {
+    for (size_t i = 0; i < n; i++) dst[i] = oracle_e4m3_to_i8(src[i], scale);
+}
+
+/* gemm_int8_wmma, src/gemm.cu:58-70: D[M x N] = sum_k A8[m][k] * B8[n][k] with
+ * 32-bit integer accumulation (B8 is the reference's column-major B, [N x K]
+ * row-major).  Summed in 64 bits and wrapped to 32, as a 32-bit accumulator
+ * wraps. */
+void oracle_gemm_i8(const int8_t* A, const int8_t* B, int32_t* D, int M, int N, int K, int nthreads) {
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1)
+#endif
+    for (int m = 0; m < M; m++) {
+        for (int n = 0; n < N; n++) {
+            int64_t s = 0;
+            for (int k = 0; k < K; k++) s += (int64_t)A[(size_t)m * K + k] * (int64_t)B[(size_t)n * K + k];
+            D[(size_t)m * N + n] = (int32_t)(uint32_t)(uint64_t)s;
+        }
+    }
+    (void)nthreads;
+}

@@ -45,6 +45,11 @@ void oracle_quantize(int fmt, const float* src, void* dst, size_t n, float scale
 void oracle_gemm(int a_fmt, const void* A, int b_fmt, const void* B, void* D, int M, int N, int K, int row0, int row1,
                  float alpha, int out_f16, int nthreads);
 
+/* INT8 path (src/gemm.cu:35-41, 58-70). */
+int8_t oracle_e4m3_to_i8(uint8_t c, float scale);
+void oracle_decode_e4m3_i8(const uint8_t* src, int8_t* dst, size_t n, float scale);
+void oracle_gemm_i8(const int8_t* A, const int8_t* B, int32_t* D, int M, int N, int K, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

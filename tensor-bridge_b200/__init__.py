@@ -99,6 +99,12 @@ SIGNATURES = {
     "tb_fp4_repack_hw": (_st, [_p, _p, _sz, _p]),
     "tb_gemm_fp8_fused_fp16": (_st, [_p, _p, _p, _i, _i, _i, _p, _sz, _p]),
     "tb_gemm_fp8_fused_workspace": (_sz, [_i, _i, _i]),
+    "tb_decode_e4m3_to_i8": (_st, [_p, _p, _sz, _f, _p]),
+    "tb_decode_e4m3_to_i8_transposed": (_st, [_p, _p, _i, _i, _f, _p]),
+    "tb_decode_fp8_to_int8": (_st, [_p, _p, _p, _p, _i, _i, _i, _f, _p]),
+    "tb_gemm_i8": (_st, [_p, _p, _p, _i, _i, _i, _p]),
+    "tb_gemm_fp8_fused_int8": (_st, [_p, _p, _p, _i, _i, _i, _f, _p, _sz, _p]),
+    "tb_gemm_fp8_fused_int8_workspace": (_sz, [_i, _i, _i]),
     "tb_gemm_sharded_fused": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _i, _p, _p]),
     "tb_nccl_unique_id": (_st, [ctypes.c_char_p]),
     "tb_nccl_comm_init": (_st, [ctypes.POINTER(_p), _i, _i, ctypes.c_char_p]),
@@ -199,6 +205,26 @@ def gemm_fused_noalloc(fmt, A, B, D, M: int, N: int, K: int, out=Out.F32, alpha:
 
 def gemm_native(a_fmt, A, b_fmt, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):
     call("tb_gemm_native", int(a_fmt), _ptr(A), int(b_fmt), _ptr(B), _ptr(D), M, N, K, int(out), alpha,
+         _stream(stream))
+
+
+def decode_e4m3_to_i8(src, dst, n: int, scale: float, stream=None):
+    """E4M3 codes -> INT8 with the reference's integer-path conversion."""
+    call("tb_decode_e4m3_to_i8", _ptr(src), _ptr(dst), n, scale, _stream(stream))
+
+
+def decode_e4m3_to_i8_transposed(src, dst, rows: int, cols: int, scale: float, stream=None):
+    call("tb_decode_e4m3_to_i8_transposed", _ptr(src), _ptr(dst), rows, cols, scale, _stream(stream))
+
+
+def gemm_i8(A, B, D, M: int, N: int, K: int, stream=None):
+    """D [M x N] INT32 = A [M x K] INT8 * B [N x K] INT8 ^T (tcgen05 kind::i8)."""
+    call("tb_gemm_i8", _ptr(A), _ptr(B), _ptr(D), M, N, K, _stream(stream))
+
+
+def gemm_fp8_fused_int8(A, B, D, M: int, N: int, K: int, scale: float, workspace, workspace_bytes: int,
+                        stream=None):
+    call("tb_gemm_fp8_fused_int8", _ptr(A), _ptr(B), _ptr(D), M, N, K, scale, _ptr(workspace), workspace_bytes,
          _stream(stream))
 
 

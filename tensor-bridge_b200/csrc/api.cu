@@ -284,6 +284,74 @@ size_t tb_gemm_fp8_fused_workspace(int M, int N, int K) {
     return bt + tb_gemm_fused_workspace(TB_FMT_E4M3, M, N, K);
 }
 
+// ---- INT8 path -------------------------------------------------------------------
+
+tb_status tb_decode_e4m3_to_i8(const uint8_t* src, int8_t* dst, size_t n, float scale, tb_stream_t stream) {
+    if (n == 0) return TB_OK;
+    if (!src || !dst) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    const int sms = tb::device_info(tb::current_device()).sms;
+    return from_cuda(tb::decode_e4m3_i8_launch(src, dst, n, scale, stream, sms), "INT8 decode launch");
+}
+
+tb_status tb_decode_e4m3_to_i8_transposed(const uint8_t* src, int8_t* dst, int rows, int cols, float scale,
+                                          tb_stream_t stream) {
+    if (rows < 0 || cols < 0) return fail(TB_ERR_SHAPE, "negative shape");
+    if (rows == 0 || cols == 0) return TB_OK;
+    if (!src || !dst) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    return from_cuda(tb::decode_e4m3_i8_transposed_launch(src, dst, rows, cols, scale, stream),
+                     "transposed INT8 decode launch");
+}
+
+tb_status tb_decode_fp8_to_int8(const uint8_t* A, const uint8_t* B, int8_t* A8, int8_t* B8, int M, int N, int K,
+                                float scale, tb_stream_t stream) {
+    if (M < 0 || N < 0 || K < 0) return fail(TB_ERR_SHAPE, "negative shape");
+    if ((A == nullptr) != (A8 == nullptr) || (B == nullptr) != (B8 == nullptr))
+        return fail(TB_ERR_INVALID_ARGUMENT, "each operand needs both its source and destination");
+    tb_status s = TB_OK;
+    if (A) s = tb_decode_e4m3_to_i8(A, A8, static_cast<size_t>(M) * K, scale, stream);
+    if (s == TB_OK && B) s = tb_decode_e4m3_to_i8_transposed(B, B8, K, N, scale, stream);
+    return s;
+}
+
+tb_status tb_gemm_i8(const int8_t* A, const int8_t* B, int32_t* D, int M, int N, int K, tb_stream_t stream) {
+    tb_status s = check_gemm_shape(M, N, K, TB_FMT_E4M3);
+    if (s != TB_OK) return s;
+    if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    if (!aligned16(A) || !aligned16(B)) return fail(TB_ERR_ALIGNMENT, "A and B must be 16-byte aligned");
+    s = check_device();
+    if (s != TB_OK) return s;
+    tb::GemmRequest r{};
+    r.kind = tb::GemmKind::kInt8;
+    r.A = A; r.B = B; r.D = D; r.ldd = N;
+    r.M = M; r.N = N; r.K = K;
+    r.alpha = 1.0f;
+    return launch_gemm(r, stream);
+}
+
+size_t tb_gemm_fp8_fused_int8_workspace(int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return (static_cast<size_t>(M) * K + 255) / 256 * 256 + (static_cast<size_t>(N) * K + 255) / 256 * 256;
+}
+
+tb_status tb_gemm_fp8_fused_int8(const uint8_t* A, const uint8_t* B, int32_t* D, int M, int N, int K, float scale,
+                                 void* workspace, size_t workspace_bytes, tb_stream_t stream) {
+    tb_status s = check_gemm_shape(M, N, K, TB_FMT_E4M3);
+    if (s != TB_OK) return s;
+    if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    const size_t need = tb_gemm_fp8_fused_int8_workspace(M, N, K);
+    if (!workspace || workspace_bytes < need) return fail(TB_ERR_WORKSPACE, "workspace needs at least %zu bytes", need);
+    if (!aligned16(workspace)) return fail(TB_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+    int8_t* A8 = static_cast<int8_t*>(workspace);
+    int8_t* B8 = A8 + (static_cast<size_t>(M) * K + 255) / 256 * 256;
+    s = tb_decode_fp8_to_int8(A, B, A8, B8, M, N, K, scale, stream);
+    if (s != TB_OK) return s;
+    return tb_gemm_i8(A8, B8, D, M, N, K, stream);
+}
+
 tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, int M, int N, int K, void* workspace,
                                  size_t workspace_bytes, tb_stream_t stream) {
     tb_status s = check_gemm_shape(M, N, K, TB_FMT_E4M3);

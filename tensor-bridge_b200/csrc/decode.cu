@@ -143,6 +143,85 @@ __global__ void __launch_bounds__(256) k_decode_transposed(const void* __restric
     }
 }
 
+// ---- FP8 E4M3 -> INT8 (the reference's integer tensor-core path) ----------------
+
+// One E4M3 code -> INT8 as src/gemm.cu:35-41 computes it:
+// (int8_t)__float2int_rn(__half2float(fp8_e4m3_to_half(c)) * scale) -- the FP16
+// decode, an FP32 product, round to nearest even into an int32 (the conversion
+// clamps to the int32 range and gives 0 for NaN), and the low byte of that.
+__device__ __forceinline__ uint32_t e4m3_to_i8_byte(uint16_t h, float scale) {
+    return static_cast<uint32_t>(__float2int_rn(__half2float(__ushort_as_half(h)) * scale)) & 0xFFu;
+}
+
+// Four codes (byte 0 first) -> four INT8 values in the same byte order.
+__device__ __forceinline__ uint32_t e4m3x4_to_i8x4(uint32_t w, float scale) {
+    uint32_t h01, h23;
+    decode_e4m3_x4(w, h01, h23);
+    return e4m3_to_i8_byte(static_cast<uint16_t>(h01), scale) |
+           (e4m3_to_i8_byte(static_cast<uint16_t>(h01 >> 16), scale) << 8) |
+           (e4m3_to_i8_byte(static_cast<uint16_t>(h23), scale) << 16) |
+           (e4m3_to_i8_byte(static_cast<uint16_t>(h23 >> 16), scale) << 24);
+}
+
+// Streamer: 16 codes -> 16 INT8 per item, warp chunks of 32 x 4 consecutive
+// items (contiguous 16-byte loads and stores); elements past the last whole
+// item one per thread.
+__global__ void __launch_bounds__(256) k_decode_e4m3_i8(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                        size_t items, const uint8_t* __restrict__ tail_src,
+                                                        uint8_t* __restrict__ tail_dst, size_t tail_begin, size_t n,
+                                                        float scale) {
+    constexpr int kRep = 4;
+    constexpr size_t kChunk = 32 * kRep;
+    const int lane = threadIdx.x & 31;
+    const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const size_t nwarps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+    for (size_t base = warp * kChunk; base < items; base += nwarps * kChunk) {
+        uint4 in[kRep];
+#pragma unroll
+        for (int j = 0; j < kRep; ++j)
+            if (base + j * 32 + lane < items) in[j] = __ldcs(src + base + j * 32 + lane);
+#pragma unroll
+        for (int j = 0; j < kRep; ++j)
+            if (base + j * 32 + lane < items)
+                dst[base + j * 32 + lane] = make_uint4(e4m3x4_to_i8x4(in[j].x, scale), e4m3x4_to_i8x4(in[j].y, scale),
+                                                       e4m3x4_to_i8x4(in[j].z, scale), e4m3x4_to_i8x4(in[j].w, scale));
+    }
+    const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (tail_begin + gt < n)
+        tail_dst[tail_begin + gt] =
+            static_cast<uint8_t>(e4m3_to_i8_byte(tensor_bridge::e4m3_to_half_bits(tail_src[tail_begin + gt]), scale));
+}
+
+// src [rows x cols] -> dst [cols x rows] (the reference's B8[col * K + k]),
+// through a 64-row x 32-column shared-memory tile as k_decode_transposed.
+__global__ void __launch_bounds__(256) k_decode_e4m3_i8_transposed(const uint8_t* __restrict__ src,
+                                                                   uint8_t* __restrict__ dst, int rows, int cols,
+                                                                   float scale) {
+    __shared__ uint8_t tile[32][64 + 4];
+    const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int r = r0 + ty + 8 * k, c = c0 + tx;
+        if (r < rows && c < cols)
+            tile[tx][ty + 8 * k] = static_cast<uint8_t>(
+                e4m3_to_i8_byte(tensor_bridge::e4m3_to_half_bits(src[static_cast<size_t>(r) * cols + c]), scale));
+    }
+    __syncthreads();
+    // Each warp writes 64 consecutive bytes of an output row, two per lane.
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int oc = ty + 8 * k;
+        const int c = c0 + oc;
+        const int r = r0 + 2 * tx;
+        if (c < cols) {
+            uint8_t* out = dst + static_cast<size_t>(c) * rows + r;
+            if (r < rows) out[0] = tile[oc][2 * tx];
+            if (r + 1 < rows) out[1] = tile[oc][2 * tx + 1];
+        }
+    }
+}
+
 // Nibble swap (reference FP4 packing <-> tensor-core packing).
 __global__ void __launch_bounds__(256) k_fp4_repack(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                                     size_t n) {
@@ -231,6 +310,28 @@ cudaError_t decode_transposed_launch(int fmt, const void* src, uint16_t* dst, in
         case kTF32: return launch_decode_t<kTF32>(src, dst, rows, cols, st);
         default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t decode_e4m3_i8_launch(const uint8_t* src, int8_t* dst, size_t n, float scale, cudaStream_t st, int sms) {
+    uint8_t* d = reinterpret_cast<uint8_t*>(dst);
+    const bool aligned = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(d)) & 15u) == 0;
+    const size_t items = aligned ? n / 16 : 0;
+    const size_t tail_begin = items * 16;
+    // Without alignment every element is a tail element: one per thread.
+    const size_t want = aligned ? (items + 1023) / 1024 : (n - tail_begin + 255) / 256;
+    size_t blocks = std::min<size_t>(std::max<size_t>(want, 1), static_cast<size_t>(sms) * 8);
+    if (!aligned) blocks = std::max<size_t>(want, 1);
+    k_decode_e4m3_i8<<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const uint4*>(src),
+                                                                     reinterpret_cast<uint4*>(d), items, src, d,
+                                                                     tail_begin, n, scale);
+    return cudaGetLastError();
+}
+
+cudaError_t decode_e4m3_i8_transposed_launch(const uint8_t* src, int8_t* dst, int rows, int cols, float scale,
+                                             cudaStream_t st) {
+    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
+    k_decode_e4m3_i8_transposed<<<grid, 256, 0, st>>>(src, reinterpret_cast<uint8_t*>(dst), rows, cols, scale);
+    return cudaGetLastError();
 }
 
 cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms) {

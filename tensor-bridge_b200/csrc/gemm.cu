@@ -172,11 +172,11 @@ static int choose_splits(int units, int num_kb, int sms) {
     return std::max(s, 1);
 }
 
-static int kb_elems(GemmKind kind) { return kind == GemmKind::kNative ? 128 : 64; }
+static int kb_elems(GemmKind kind) { return kind == GemmKind::kNative || kind == GemmKind::kInt8 ? 128 : 64; }
 
 size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int sms) {
     (void)a_fmt;
-    if (M <= 0 || N <= 0 || K <= 0 || kind == GemmKind::kNative) return 0;
+    if (M <= 0 || N <= 0 || K <= 0 || kind == GemmKind::kNative || kind == GemmKind::kInt8) return 0;
     const int bn = choose_bn(N);
     const int units = ((M + 127) / 128) * ((N + bn - 1) / bn);
     const int num_kb = (K + kb_elems(kind) - 1) / kb_elems(kind);
@@ -197,6 +197,8 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
                             CU_TENSOR_MAP_SWIZZLE_128B);
     } else if constexpr (MODE == kModeNative8) {
         ok = make_native_map(&ta, r.a_fmt, r.A, K, r.M, 128) && make_native_map(&tbm, r.b_fmt, r.B, K, r.N, BN);
+    } else if constexpr (MODE == kModeInt8) {
+        ok = make_native_map(&ta, kE4M3, r.A, K, r.M, 128) && make_native_map(&tbm, kE4M3, r.B, K, r.N, BN);
     } else {
         // Raw A: 128-byte boxes, 128-byte swizzle (the decode warps read the
         // swizzled layout).
@@ -297,7 +299,7 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     const int tiles_n = (r.N + bn - 1) / bn;
     const int num_kb = (r.K + kb_elems(r.kind) - 1) / kb_elems(r.kind);
     int splits = 1;
-    if (r.kind != GemmKind::kNative) {
+    if (r.kind != GemmKind::kNative && r.kind != GemmKind::kInt8) {
         splits = r.force_splits ? r.force_splits : choose_splits(tiles_m * tiles_n, num_kb, sms);
         splits = std::max(1, std::min(splits, num_kb));
     }
@@ -322,6 +324,8 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     a.alpha = r.alpha;
     a.D = r.D; a.ldd = r.ldd;
     a.out_f16 = r.out_f16;
+    a.out_i32 = r.kind == GemmKind::kInt8 ? 1 : 0;
+    if (a.out_i32) a.tx_bytes = 128u * 128u + static_cast<uint32_t>(bn) * 128u;
     const int vec_elems = r.out_f16 ? 8 : 4;
     a.vec_ok = ((reinterpret_cast<uintptr_t>(r.D) & 15u) == 0 && (r.ldd % vec_elems) == 0) ? 1 : 0;
     a.ws = splits > 1 ? static_cast<float*>(r.workspace) : nullptr;
@@ -343,6 +347,12 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
             else if (bn == 64) e = run<64, kModeNative8, kE4M3>(r, a, st, dev, why);
             else if (bn == 128) e = run<128, kModeNative8, kE4M3>(r, a, st, dev, why);
             else e = run<256, kModeNative8, kE4M3>(r, a, st, dev, why);
+            break;
+        case GemmKind::kInt8:
+            if (bn == 16) e = run<16, kModeInt8, kE4M3>(r, a, st, dev, why);
+            else if (bn == 64) e = run<64, kModeInt8, kE4M3>(r, a, st, dev, why);
+            else if (bn == 128) e = run<128, kModeInt8, kE4M3>(r, a, st, dev, why);
+            else e = run<256, kModeInt8, kE4M3>(r, a, st, dev, why);
             break;
         case GemmKind::kFused:
             switch (r.a_fmt) {

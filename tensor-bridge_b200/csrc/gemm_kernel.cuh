@@ -56,7 +56,7 @@
 
 namespace tb {
 
-enum : int { kModeF16 = 0, kModeDecode = 1, kModeNative8 = 2 };
+enum : int { kModeF16 = 0, kModeDecode = 1, kModeNative8 = 2, kModeInt8 = 3 };
 
 // Stored-format ids (same values as tb_format in the C header).
 enum : int { kF16 = 0, kE4M3 = 1, kE5M2 = 2, kE2M1 = 3, kE2M1U = 4, kBF16 = 5, kTF32 = 6, kE2M1HW = 7 };
@@ -94,6 +94,8 @@ struct GemmCfg {
     static constexpr int MODE = MODE_;
     static constexpr int FMT = FMT_;
     static constexpr bool kDecode = MODE == kModeDecode;
+    // Both operands loaded raw by TMA, 128-value k-blocks (kind::f8f6f4, kind::i8).
+    static constexpr bool kNativeLike = MODE == kModeNative8 || MODE == kModeInt8;
     static constexpr int S = S_;
     static constexpr int SA = kDecode ? SA_ : 0;
     static constexpr int ND = kDecode ? 8 : 0;  // decode warps
@@ -114,7 +116,7 @@ struct GemmCfg {
     static constexpr int RSTAGE_BYTES = RA_BYTES + (BRAW ? RK * BN * 128 : 0);
     static constexpr int FULL_COUNT = (BRAW ? 0 : 1) + ND;
     // K elements per k-block and the TMA inner-coordinate steps.
-    static constexpr int KB_ELEMS = MODE == kModeNative8 ? 128 : 64;
+    static constexpr int KB_ELEMS = kNativeLike ? 128 : 64;
     static constexpr int B_X_STEP = KB_ELEMS;
 
     // Shared-memory layout (offsets from a 1024-byte aligned base).
@@ -130,14 +132,15 @@ struct GemmCfg {
     // NACC accumulators in turn, summed by the epilogue.  Narrow tiles make
     // each MMA short, and MMAs into one accumulator run back to back at MMA
     // latency; separate chains overlap.
-    static constexpr int NACC = BN <= 64 ? 4 : (BN <= 128 ? 2 : 1);
+    // (kind::i8 accumulates integers exactly and keeps one chain.)
+    static constexpr int NACC = MODE == kModeInt8 ? 1 : (BN <= 64 ? 4 : (BN <= 128 ? 2 : 1));
     static constexpr int TMEM_COLS = pow2_at_least(2 * NACC * BN);
     static constexpr int CW = BN < 32 ? BN : 32;  // epilogue column chunk
 
     // MMA: kind::f16 with FP16 operands, or kind::f8f6f4 (operand formats
     // OR'd in at run time from GemmArgs::idesc_ab), FP32 accumulation,
     // K-major operands.
-    static constexpr uint32_t IDESC = idesc_make(0u, 0u, BM, BN);
+    static constexpr uint32_t IDESC = MODE == kModeInt8 ? idesc_i8(BM, BN) : idesc_make(0u, 0u, BM, BN);
 
     // Decode work per k-block: 16-byte raw units per row and in total, and
     // units per decode thread.
@@ -164,6 +167,7 @@ struct GemmArgs {
     long long ldd;
     int out_f16;     // 1: FP16 output, 0: FP32
     int vec_ok;      // 1: D rows allow 16-byte vector stores
+    int out_i32;     // 1: D is INT32 (kind::i8), stored as accumulated, no alpha
     float* ws;       // split-K partials [splits][M][N] (FP32), when splits > 1
     uint32_t idesc_ab;  // native mode: A/B format fields of the instruction descriptor
     uint32_t tx_bytes;  // native mode: TMA bytes per operand stage (packed FP4 counts 64 per 128-value row)
@@ -291,6 +295,18 @@ template <int CW>
 __device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int sp, int row, int col0, const uint32_t (&v)[CW]) {
     if (row >= p.M) return;
     const bool full = col0 + CW <= p.N;
+    if (p.out_i32) {
+        uint32_t* dst = static_cast<uint32_t*>(p.D) + static_cast<size_t>(row) * p.ldd + col0;
+        if (full && p.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < CW; j += 4) *reinterpret_cast<uint4*>(dst + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < CW; ++j)
+                if (col0 + j < p.N) dst[j] = v[j];
+        }
+        return;
+    }
     if (p.splits > 1) {
         float* dst = p.ws + (static_cast<size_t>(sp) * p.M + row) * static_cast<size_t>(p.N) + col0;
         if (full && (p.N & 3) == 0) {
@@ -413,7 +429,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             long long issued = 0;
             bool ok = true;
             const uint32_t kTx =
-                C::MODE == kModeNative8 ? p.tx_bytes : C::B_BYTES + (C::kDecode ? 0u : static_cast<uint32_t>(C::A_BYTES));
+                C::kNativeLike ? p.tx_bytes : C::B_BYTES + (C::kDecode ? 0u : static_cast<uint32_t>(C::A_BYTES));
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
                 int tm, tn, sp, kb0, kb1;
                 unit_coords(p, u, tm, tn, sp);
@@ -467,6 +483,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                             const uint64_t ad = sdesc_make(a_lo + 2u * kk), bd = sdesc_make(b_lo + 2u * kk);
                             if constexpr (C::MODE == kModeNative8)
                                 mma_f8f6f4_ss(d, ad, bd, C::IDESC | p.idesc_ab, accum);
+                            else if constexpr (C::MODE == kModeInt8)
+                                mma_i8_ss(d, ad, bd, C::IDESC, accum);
                             else mma_f16_ss(d, ad, bd, C::IDESC, accum);
                         }
                         mma_commit(&b_empty[bs]);

@@ -13,6 +13,9 @@ namespace tb {
 cudaError_t decode_launch(int fmt, const void* src, uint16_t* dst, size_t n, cudaStream_t st, int sms);
 cudaError_t decode_transposed_launch(int fmt, const void* src, uint16_t* dst, int rows, int cols, cudaStream_t st);
 cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms);
+cudaError_t decode_e4m3_i8_launch(const uint8_t* src, int8_t* dst, size_t n, float scale, cudaStream_t st, int sms);
+cudaError_t decode_e4m3_i8_transposed_launch(const uint8_t* src, int8_t* dst, int rows, int cols, float scale,
+                                             cudaStream_t st);
 size_t stored_bytes(int fmt, size_t n);
 
 // quantize.cu
@@ -20,7 +23,7 @@ cudaError_t quantize_launch(int fmt, const float* src, void* dst, size_t n, floa
 cudaError_t absmax_launch(const float* src, size_t n, float* out, cudaStream_t st, int sms);
 
 // gemm.cu
-enum class GemmKind { kF16, kFused, kNative };
+enum class GemmKind { kF16, kFused, kNative, kInt8 };
 
 struct GemmRequest {
     GemmKind kind;

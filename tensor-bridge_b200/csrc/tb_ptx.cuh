@@ -198,6 +198,18 @@ __device__ __forceinline__ void mma_f8f6f4_ss(uint32_t d_tmem, uint64_t adesc, u
         : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8: signed 8-bit operands, S32
+// accumulation (exact), K = 32 per instruction.
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16: the A operand is read from
 // tensor memory (M = 128 rows in the 128 lanes, K = 16 values in 8 columns
 // starting at a_tmem, two FP16 values per 32-bit column, lower K in the low
@@ -325,6 +337,13 @@ __device__ __forceinline__ uint64_t sdesc_make(uint32_t lo) {
 // Instruction descriptor (kind::f16 / kind::f8f6f4, dense): D format F32,
 // both operands K-major, shape M x N.  a_fmt/b_fmt: for kind::f16 0 = F16,
 // 1 = BF16; for kind::f8f6f4 0 = E4M3, 1 = E5M2, 5 = E2M1.
+// Instruction descriptor for kind::i8: D format S32 (2), both operands
+// signed 8-bit (1), K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 __host__ __device__ constexpr uint32_t idesc_make(uint32_t a_fmt, uint32_t b_fmt, int m, int n) {
     return (1u << 4)                                  // D = F32
            | (a_fmt << 7) | (b_fmt << 10)             // operand formats
