@@ -21,7 +21,8 @@
 //               moving full 128-byte lines.  The decode warps free a raw stage
 //               as soon as they have read it, so raw A is prefetched
 //               independently of the MMA.
-//   warps 7-14  decode warps: for each k-block (in rounds of DK), read its slice of the staged
+//   warps 7-    decode warps (8, or 16 for the wide tiles of the one-byte and
+//               wider formats): for each k-block (in rounds of DK), read its slice of the staged
 //               raw tile, decode it to FP16 and write it, 128-byte swizzled,
 //               into the A tile of the operand-ring stage that the MMA reads
 //               directly; decoded weights never leave shared memory.  The
@@ -98,7 +99,10 @@ struct GemmCfg {
     static constexpr bool kNativeLike = MODE == kModeNative8 || MODE == kModeInt8;
     static constexpr int S = S_;
     static constexpr int SA = kDecode ? SA_ : 0;
-    static constexpr int ND = kDecode ? 8 : 0;  // decode warps
+    // Decode warps: 16 for the wide tiles of the formats with at least 64 raw
+    // bytes per k-block row (E4M3, E5M2, BF16, TF32: their decode, not the
+    // MMA, bounds the fused kernel there); 8 otherwise.
+    static constexpr int ND = kDecode ? ((BN >= 128 && raw_row_bytes(FMT) >= 64) ? 16 : 8) : 0;
     static constexpr int DECODE_WARP0 = 7;
     static constexpr int NUM_THREADS = kDecode ? (DECODE_WARP0 + ND) * 32 : 192;
     static constexpr int DECODE_THREADS = ND * 32;
@@ -146,7 +150,7 @@ struct GemmCfg {
     // units per decode thread.
     static constexpr int U_ROW = kDecode ? raw_row_bytes(FMT) / 16 : 1;
     static constexpr int UNITS = 128 * U_ROW;
-    static constexpr int UPT = UNITS / 256;
+    static constexpr int UPT = UNITS / (ND > 0 ? ND * 32 : 256);
 
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "BN");
     static_assert(B_BYTES % 1024 == 0 && RA_BYTES % 1024 == 0 && RSTAGE_BYTES % 1024 == 0, "stage alignment");
