@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include "fused_tmem_kernel.cuh"
+#include "gemm_pair_kernel.cuh"
 #include "gemm_kernel.cuh"
 #include "tb_host.h"
 
@@ -185,6 +186,76 @@ size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int s
     return static_cast<size_t>(s) * M * N * sizeof(float);
 }
 
+// ---- pairs of SMs (cta_group::2) for the operand-loading modes ------------------------
+
+template <int MODE>
+using PairOf = PairCfg<MODE, 6>;
+
+// Clusters of two that fit on the device at once (0 if the query fails).
+template <int MODE>
+static int pair_clusters(int dev) {
+    using C = PairOf<MODE>;
+    static std::atomic<int> cached[64] = {};
+    if (dev < 0 || dev >= 64) return 0;
+    int v = cached[dev].load();
+    if (v) return v > 0 ? v : 0;
+    int n = 0;
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * 128, 1, 1);
+    cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaFuncSetAttribute(k_gemm_pair<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, k_gemm_pair<C>, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+    }
+    cached[dev].store(n > 0 ? n : -1);
+    return n;
+}
+
+template <int MODE>
+static cudaError_t run_pair(const GemmRequest& r, const GemmArgs& args, int clusters, cudaStream_t st,
+                            const char** why) {
+    using C = PairOf<MODE>;
+    CUtensorMap ta, tbm;
+    const uint64_t K = static_cast<uint64_t>(r.K);
+    bool ok;
+    if constexpr (MODE == kModeF16) {
+        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
+             make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else if constexpr (MODE == kModeNative8) {
+        ok = make_native_map(&ta, r.a_fmt, r.A, K, r.M, 128) && make_native_map(&tbm, r.b_fmt, r.B, K, r.N, 128);
+    } else {
+        ok = make_native_map(&ta, kE4M3, r.A, K, r.M, 128) && make_native_map(&tbm, kE4M3, r.B, K, r.N, 128);
+    }
+    if (!ok) {
+        *why = "cuTensorMapEncodeTiled rejected the operand layout";
+        return cudaErrorInvalidValue;
+    }
+    const int units = ((r.M + C::BM - 1) / C::BM) * ((r.N + C::BN - 1) / C::BN);
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * std::min(units, clusters), 1, 1);
+    cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_gemm_pair<C>, ta, tbm, args);
+}
+
 template <int BN, int MODE, int FMT>
 static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t st, int dev, const char** why) {
     using C = typename Pick<BN, MODE, FMT>::Cfg;
@@ -337,6 +408,29 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
         // (64 per 128-value row), not the padded bytes it writes.
         auto row_bytes = [](int f) { return f == kE2M1HW ? 64u : 128u; };
         a.tx_bytes = 128u * row_bytes(r.a_fmt) + static_cast<uint32_t>(bn) * row_bytes(r.b_fmt);
+    }
+
+    // Pairs of SMs for the operand-loading kinds when the tiles are wide and
+    // plentiful (one 256 x 256 tile per cluster, no split).
+    const bool loading = r.kind == GemmKind::kF16 || r.kind == GemmKind::kNative || r.kind == GemmKind::kInt8;
+    if (loading && bn == 256 && splits == 1 && r.M >= 256 && !r.force_bn && !r.force_splits) {
+        const int mode = r.kind == GemmKind::kF16 ? kModeF16 : r.kind == GemmKind::kNative ? kModeNative8 : kModeInt8;
+        const int clusters = mode == kModeF16 ? pair_clusters<kModeF16>(dev)
+                             : mode == kModeNative8 ? pair_clusters<kModeNative8>(dev)
+                                                    : pair_clusters<kModeInt8>(dev);
+        if (clusters > 0) {
+            // Bytes each CTA stages per k-block: 128 rows of A and 128 of B.
+            auto row_bytes = [&](int f) -> uint32_t {
+                return r.kind == GemmKind::kF16 ? 128u : (f == kE2M1HW ? 64u : 128u);
+            };
+            a.tx_bytes = 128u * row_bytes(r.a_fmt) + 128u * row_bytes(r.kind == GemmKind::kNative ? r.b_fmt : r.a_fmt);
+            if (r.kind == GemmKind::kInt8) a.tx_bytes = 2u * 128u * 128u;
+            if (r.kind != GemmKind::kNative) a.idesc_ab = 0;
+            cudaError_t e2 = mode == kModeF16 ? run_pair<kModeF16>(r, a, clusters, st, why)
+                             : mode == kModeNative8 ? run_pair<kModeNative8>(r, a, clusters, st, why)
+                                                    : run_pair<kModeInt8>(r, a, clusters, st, why);
+            return e2;
+        }
     }
 
     cudaError_t e;
