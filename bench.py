@@ -713,6 +713,15 @@ def profile_case(case: str):
     tb = load_package()
     fname, shape = case.split(":")
     M, N, K = (int(v) for v in shape.lower().split("x"))
+    if fname == "f16":  # the plain FP16 GEMM
+        A = torch.randn(M, K, device="cuda").half()
+        B = torch.randn(N, K, device="cuda").half()
+        D = torch.empty(M, N, dtype=torch.float32, device="cuda")
+        for _ in range(5):
+            tb.gemm_f16(A, B, D, M, N, K)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": case, "ok": True}))
+        return
     fmt = {"e4m3": tb.Format.E4M3, "e2m1": tb.Format.E2M1, "bf16": tb.Format.BF16, "tf32": tb.Format.TF32}[fname]
     if fname in FORMAT_MAX:
         A, alpha = weights_q(torch, tb, fmt, M, K, 0.02, seed=1)
@@ -742,7 +751,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the MLP-shape and 8192^3 FP4 sub-objects")
     ap.add_argument("--profile-case", metavar="FMT:MxNxK",
-                    help="run only 5 fused weight-only GEMMs of this case (e.g. e4m3:14336x16x4096) and exit; "
+                    help="run only 5 fused weight-only GEMMs of this case (e.g. e4m3:14336x16x4096; f16:MxNxK for "
+                         "the plain FP16 GEMM) and exit; "
                          "the command profiles/ captures of single kernels use")
     args = ap.parse_args()
     if args.profile_case:
@@ -826,10 +836,14 @@ def main():
         "formats": formats,
     }
     if not args.no_extra:
+        extra_clocks = ClockSampler(dist.local)
+        extra_clocks.start()
         line["decode_stream_14336x4096"] = decode_streams(torch, tb, peaks)
         line["weight_only_mlp"] = mlp_weight_only(torch, tb, peaks)
         line["fp4_8192_fused"] = fp4_square(torch, tb, peaks)
         line["int8_4096"] = int8_square(torch, tb)
+        # clocks over the extra sections (the headline's own are in "clocks")
+        line["clocks_extras"] = extra_clocks.stop()
         line["sharded_weight_gemm"] = sharded_weight_gemm(torch, tb, dist)
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline((M, N, K))
