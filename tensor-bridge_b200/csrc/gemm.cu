@@ -6,6 +6,7 @@
 #include <mutex>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include "fused_pair_kernel.cuh"
 #include "fused_tmem_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
 #include "gemm_kernel.cuh"
@@ -114,6 +115,21 @@ static int f8f6f4_code(int fmt) {
     }
 }
 
+// Tensor map of a stored-format A [M x K] for the fused kernels: 128-byte
+// boxes of 128 rows, 128-byte swizzle (the decode warps read that layout).
+template <int FMT>
+static bool make_raw_map(CUtensorMap* m, const void* A, uint64_t K, uint64_t M) {
+    constexpr uint32_t bx = raw_box_elems(FMT);
+    if constexpr (FMT == kE2M1)
+        return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K / 2, M, K / 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    else if constexpr (FMT == kBF16)
+        return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, A, K, M, K * 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    else if constexpr (FMT == kTF32)
+        return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, A, K, M, K * 4, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    else
+        return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, K, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 // ---------------------------------------------------------------------------------
 // Configurations
 
@@ -191,10 +207,10 @@ size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int s
 template <int MODE>
 using PairOf = PairCfg<MODE, 6>;
 
-// Clusters of two that fit on the device at once (0 if the query fails).
-template <int MODE>
-static int pair_clusters(int dev) {
-    using C = PairOf<MODE>;
+// Clusters of two CTAs of `kernel` (configuration C) that fit on the device at
+// once (0 if the query fails); also sets the kernel's shared-memory size.
+template <class C, class Kern>
+static int cluster_capacity(Kern kernel, int dev) {
     static std::atomic<int> cached[64] = {};
     if (dev < 0 || dev >= 64) return 0;
     int v = cached[dev].load();
@@ -211,14 +227,38 @@ static int pair_clusters(int dev) {
     cfg.dynamicSmemBytes = C::SMEM_ALLOC;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    if (cudaFuncSetAttribute(k_gemm_pair<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC) !=
-            cudaSuccess ||
-        cudaOccupancyMaxActiveClusters(&n, k_gemm_pair<C>, &cfg) != cudaSuccess) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
         (void)cudaGetLastError();
         n = 0;
     }
     cached[dev].store(n > 0 ? n : -1);
     return n;
+}
+
+template <int MODE>
+static int pair_clusters(int dev) {
+    using C = PairOf<MODE>;
+    return cluster_capacity<C>(k_gemm_pair<C>, dev);
+}
+
+// Launch of a two-CTA-cluster kernel over `units` pair tiles.
+template <class C, class Kern>
+static cudaError_t launch_pairs(Kern kernel, const CUtensorMap& ta, const CUtensorMap& tbm, const GemmArgs& args,
+                                int units, int clusters, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * std::min(units, clusters), 1, 1);
+    cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, ta, tbm, args);
 }
 
 template <int MODE>
@@ -241,19 +281,78 @@ static cudaError_t run_pair(const GemmRequest& r, const GemmArgs& args, int clus
         return cudaErrorInvalidValue;
     }
     const int units = ((r.M + C::BM - 1) / C::BM) * ((r.N + C::BN - 1) / C::BN);
-    cudaLaunchConfig_t cfg{};
-    cudaLaunchAttribute attr{};
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * std::min(units, clusters), 1, 1);
-    cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
-    cfg.stream = st;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_gemm_pair<C>, ta, tbm, args);
+    return launch_pairs<C>(k_gemm_pair<C>, ta, tbm, args, units, clusters, st);
+}
+
+// Fused decode + GEMM on 256 x 512 SM-pair tiles (fused_pair_kernel.cuh):
+// four operand stages of 48 KB (this CTA's decoded A tile and 256 B rows; TF32
+// three, for two 32 KB raw stages) and the rest of shared memory for the raw
+// ring.
+template <int FMT>
+struct PickFusedPair {
+    static constexpr int S = FMT == kTF32 ? 3 : 4;
+    static constexpr int SA0 = (kSmemBudget - S * 3 * 128 * 128) / raw_stage_bytes(FMT);
+    static constexpr int SA = SA0 > 8 ? 8 : SA0;
+    static constexpr int DK = raw_kblocks(FMT) < 2 ? raw_kblocks(FMT) : 2;
+    using Cfg = FusedPairCfg<FMT, S, SA, DK>;
+};
+
+template <int FMT>
+static int fused_pair_clusters(int dev) {
+    using C = typename PickFusedPair<FMT>::Cfg;
+    return cluster_capacity<C>(k_fused_pair<C>, dev);
+}
+
+// Clusters of the fused pair kernel of this format that fit at once (0: none,
+// or a format without a pair kernel).
+static int fused_pair_capacity(int fmt, int dev) {
+    switch (fmt) {
+        case kE4M3: return fused_pair_clusters<kE4M3>(dev);
+        case kE5M2: return fused_pair_clusters<kE5M2>(dev);
+        case kE2M1: return fused_pair_clusters<kE2M1>(dev);
+        case kE2M1U: return fused_pair_clusters<kE2M1U>(dev);
+        case kBF16: return fused_pair_clusters<kBF16>(dev);
+        case kTF32: return fused_pair_clusters<kTF32>(dev);
+        default: return 0;
+    }
+}
+
+// Throughput per SM of the fused pair kernel over the one-CTA fused kernel on
+// whole waves (measured at 4096^3 on B200): the decode it halves per output
+// bounds the one-byte and wider formats; packed FP4 is bound by the MMAs.
+static double fused_pair_gain(int fmt) {
+    switch (fmt) {
+        case kE4M3: case kE5M2: return 1.19;
+        case kBF16: return 1.40;
+        case kTF32: return 1.57;
+        default: return 1.0;
+    }
+}
+
+// Pair tiles (256 x 512, on two SMs) against one-CTA tiles (128 x 256): a pair
+// tile is twice an SM's work of a one-CTA tile, so compare the waves each
+// needs, weighted by the pair kernel's gain; ties go to the pair kernel.
+static bool fused_pair_wins(int fmt, int M, int N, int clusters, int sms) {
+    const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + 511) / 512);
+    const long long one_tiles = static_cast<long long>((M + 127) / 128) * ((N + 255) / 256);
+    const long long pair_waves = (pair_tiles + clusters - 1) / clusters;
+    const long long one_waves = (one_tiles + sms - 1) / sms;
+    return 2.0 * static_cast<double>(pair_waves) / fused_pair_gain(fmt) <= static_cast<double>(one_waves) + 1e-9;
+}
+
+template <int FMT>
+static cudaError_t run_fused_pair(const GemmRequest& r, const GemmArgs& args, int clusters, cudaStream_t st,
+                                  const char** why) {
+    using C = typename PickFusedPair<FMT>::Cfg;
+    CUtensorMap ta, tbm;
+    const uint64_t K = static_cast<uint64_t>(r.K);
+    if (!make_raw_map<FMT>(&ta, r.A, K, r.M) ||
+        !make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) {
+        *why = "cuTensorMapEncodeTiled rejected the operand layout";
+        return cudaErrorInvalidValue;
+    }
+    const int units = ((r.M + C::BM - 1) / C::BM) * ((r.N + C::BN - 1) / C::BN);
+    return launch_pairs<C>(k_fused_pair<C>, ta, tbm, args, units, clusters, st);
 }
 
 template <int BN, int MODE, int FMT>
@@ -271,19 +370,7 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
     } else if constexpr (MODE == kModeInt8) {
         ok = make_native_map(&ta, kE4M3, r.A, K, r.M, 128) && make_native_map(&tbm, kE4M3, r.B, K, r.N, BN);
     } else {
-        // Raw A: 128-byte boxes, 128-byte swizzle (the decode warps read the
-        // swizzled layout).
-        constexpr uint32_t bx = raw_box_elems(FMT);
-        if constexpr (FMT == kE2M1) {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K / 2, r.M, K / 2, bx, 128,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
-        } else if constexpr (FMT == kBF16) {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-        } else if constexpr (FMT == kTF32) {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT32, r.A, K, r.M, K * 4, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-        } else {
-            ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-        }
+        ok = make_raw_map<FMT>(&ta, r.A, K, r.M);
         ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, BN,
                             CU_TENSOR_MAP_SWIZZLE_128B);
     }
@@ -315,17 +402,7 @@ static cudaError_t run_tmem(const GemmRequest& r, const GemmArgs& args, cudaStre
     using C = typename PickTmem<BN, FMT>::Cfg;
     CUtensorMap ta, tbm;
     const uint64_t K = static_cast<uint64_t>(r.K);
-    constexpr uint32_t bx = raw_box_elems(FMT);
-    bool ok;
-    if constexpr (FMT == kE2M1) {
-        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K / 2, r.M, K / 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    } else if constexpr (FMT == kBF16) {
-        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    } else if constexpr (FMT == kTF32) {
-        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT32, r.A, K, r.M, K * 4, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    } else {
-        ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, r.A, K, r.M, K, bx, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    }
+    bool ok = make_raw_map<FMT>(&ta, r.A, K, r.M);
     ok = ok && make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!ok) {
         *why = "cuTensorMapEncodeTiled rejected the operand layout";
@@ -430,6 +507,24 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
                              : mode == kModeNative8 ? run_pair<kModeNative8>(r, a, clusters, st, why)
                                                     : run_pair<kModeInt8>(r, a, clusters, st, why);
             return e2;
+        }
+    }
+
+    // Fused decode on SM pairs (256 x 512 tiles) for at least 512 columns,
+    // tiles enough not to split K, and fewer waves' worth of work than the
+    // one-CTA kernel.
+    if (r.kind == GemmKind::kFused && r.N >= 512 && splits == 1 && r.M >= 256 && !r.force_bn && !r.force_splits) {
+        const int clusters = fused_pair_capacity(r.a_fmt, dev);
+        if (clusters > 0 && fused_pair_wins(r.a_fmt, r.M, r.N, clusters, sms)) {
+            switch (r.a_fmt) {
+                case kE4M3: return run_fused_pair<kE4M3>(r, a, clusters, st, why);
+                case kE5M2: return run_fused_pair<kE5M2>(r, a, clusters, st, why);
+                case kE2M1: return run_fused_pair<kE2M1>(r, a, clusters, st, why);
+                case kE2M1U: return run_fused_pair<kE2M1U>(r, a, clusters, st, why);
+                case kBF16: return run_fused_pair<kBF16>(r, a, clusters, st, why);
+                case kTF32: return run_fused_pair<kTF32>(r, a, clusters, st, why);
+                default: break;
+            }
         }
     }
 

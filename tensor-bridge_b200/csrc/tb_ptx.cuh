@@ -155,6 +155,27 @@ __device__ __forceinline__ void mbar_arrive_cluster(const uint64_t* bar, uint32_
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
 
+// Shared::cluster address of `p` (this CTA's shared memory) in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(p)), "r"(rank));
+    return remote;
+}
+
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from
+// this CTA's shared memory to shared memory of a CTA of the cluster; its
+// completion is counted (complete_tx) on the mbarrier at `bar_cluster` there.
+// Issued through the async proxy: a cheap way to signal another CTA's
+// barrier after a proxy fence, without a cluster-scope release.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                                     uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dst_cluster),
+        "r"(smem_addr(src)), "r"(bytes), "r"(bar_cluster)
+        : "memory");
+}
+
 // TMEM allocation shared by the two CTAs: one warp with the same warp index
 // in each CTA executes it.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {

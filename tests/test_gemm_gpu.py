@@ -134,6 +134,60 @@ def test_fused_equals_unfused_bitwise(tb, cuda, fmt):
     np.testing.assert_array_equal(fused.view(np.uint32), unfused.view(np.uint32))
 
 
+# Shapes the launcher gives to the SM-pair kernel (256 x 512 pair tiles, each
+# CTA decoding its own 128 rows; chosen when at least 512 columns need no
+# split and no more waves than the one-CTA kernel): ragged M and N inside a
+# pair tile (1900 rows leave the second CTA of the last tile row no rows;
+# 3700 columns leave the last tile's second half none), K with a partial k-block
+# or a partial raw stage, several tiles per cluster.  Bit-identical to
+# decode-then-GEMM everywhere, and against the oracle on bands of rows that
+# straddle tile boundaries and on the last rows.
+PAIR_SHAPES = [(1900, 3700, 320), (2048, 4096, 96), (1024, 8192, 4160)]
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E5M2, O.E2M1, O.E2M1_UNPACKED, O.BF16, O.TF32])
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+def test_fused_pair_tiles(tb, cuda, fmt, M, N, K):
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=fmt * 5 + N)
+    got = run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha, force_ws=False)
+    unfused = run_unfused(tb, cuda, fmt, A, B16, M, N, K, alpha)
+    np.testing.assert_array_equal(got.view(np.uint32), unfused.view(np.uint32))
+    for rows in ((100, 164), (230, 290), (M - 40, M)):
+        check(got[rows[0]:rows[1]], O.gemm(fmt, A, O.F16, B16, M, N, K, rows=rows, alpha=alpha))
+
+
+def kernels_launched(cuda, fn):
+    """Names of the kernels `fn` launches (CUPTI trace through torch.profiler)."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
+        fn()
+        cuda.cuda.synchronize()
+    return {e.name for e in prof.events()}
+
+
+@pytest.mark.parametrize("M,N,K,pair", [(1900, 3700, 320, True), (2048, 4096, 96, True), (1024, 8192, 4160, True),
+                                        (4096, 2304, 1024, False), (300, 600, 640, False)])
+def test_fused_pair_choice(tb, cuda, M, N, K, pair):
+    """The pair-tile shapes above do run on the SM-pair kernel, and shapes
+    whose pair tiles would take more waves stay on the one-CTA kernel."""
+    fmt = O.E2M1
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=1)
+    dA, dB = to_dev(cuda, A), to_dev(cuda, B16)
+    dD = empty_dev(cuda, M * N * 4)
+    names = kernels_launched(cuda, lambda: tb.gemm_fused(fmt, dA, dB, dD, M, N, K, alpha=alpha))
+    assert any("k_fused_pair" in n for n in names) == pair, names
+
+
+@pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1, O.TF32])
+def test_fused_pair_tiles_f16_out(tb, cuda, fmt):
+    M, N, K = 1900, 3700, 320
+    A, B16, alpha = make_operands(fmt, M, N, K, seed=fmt * 3)
+    got = run_fused(tb, cuda, fmt, A, B16, M, N, K, alpha, out=tb.Out.F16, force_ws=False)
+    for rows in ((100, 164), (M - 40, M)):
+        want = O.f16_bits_to_f32(O.gemm(fmt, A, O.F16, B16, M, N, K, rows=rows, alpha=alpha, out_f16=True))
+        check(got[rows[0]:rows[1]], want)
+
+
 def run_unfused(tb, cuda, fmt, A, B16, M, N, K, alpha):
     dA, dB = to_dev(cuda, A), to_dev(cuda, B16)
     A16 = empty_dev(cuda, M * K * 2)
@@ -147,7 +201,7 @@ def run_unfused(tb, cuda, fmt, A, B16, M, N, K, alpha):
 # Persistent CTAs walk several output tiles each once the tile count exceeds the
 # SM count (148 on B200): these shapes give every CTA 2 to 4 tiles, so the raw
 # and operand rings wrap across tile boundaries with TMA refills that hit L2.
-MULTI_TILE = [(4096, 4096, 4096), (2048, 4096, 512), (4096, 2304, 1024), (1024, 8192, 256)]
+MULTI_TILE = [(4096, 4096, 4096), (2048, 4096, 512), (4096, 2304, 1024), (1024, 8192, 256), (4096, 8192, 192)]
 
 
 @pytest.mark.parametrize("fmt", [O.E4M3, O.E2M1, O.BF16, O.TF32])
