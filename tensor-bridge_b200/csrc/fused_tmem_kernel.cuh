@@ -300,9 +300,20 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    // The next narrow GEMM in the stream may start now: its weight stream then
+    // overlaps this kernel's tail (launched with programmatic stream
+    // serialisation; see the dependency waits below).
+    if (threadIdx.x == 0) grid_dep_launch_dependents();
 
     if (warp == 0) {
         // ---------------- TMA producer: raw A stages ----------------
+        // Weights in the one-byte and packed formats are streamed before the
+        // previous kernel has completed (when it let this one start early, as
+        // this kernel does): no kernel that triggers early writes them (this
+        // library's quantizer does not trigger, so a GEMM after it waits).
+        // BF16 and TF32 words could be an earlier GEMM's FP16 / FP32 output:
+        // wait for it first.
+        if constexpr (C::FMT == kBF16 || C::FMT == kTF32) grid_dep_wait();
         uint32_t st = 0;  // CTA-wide stage number
         bool ok = true;
         NCursor cur;
@@ -343,6 +354,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         if (!ok && lane == 0) settle_inflight_loads();
     } else if (warp == C::B_WARP) {
         // ---------------- TMA producer: the four B tiles of each round ----------------
+        // B (activations) may be the previous kernel's output: wait for it.
+        grid_dep_wait();
         uint32_t r = 0;
         bool ok = true;
         NCursor cur;
@@ -413,6 +426,9 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         }
     } else if (warp < 6) {
         // ---------------- epilogue ----------------
+        // D (or the split-K partials) may still be read or written by the
+        // previous kernel: wait for it to complete before the first store.
+        grid_dep_wait();
         const int quarter = warp & 3;
         int t = 0;
         NCursor cur;

@@ -23,6 +23,10 @@ cudaError_t device_error_clear() {
 
 __global__ void k_splitk_reduce(const float* __restrict__ ws, void* D, long long ldd, int M, int N, int splits,
                                 float alpha, int out_f16) {
+    // Launched with programmatic stream serialisation: let the next GEMM start
+    // streaming its weights, then wait for the partials of the GEMM before.
+    grid_dep_launch_dependents();
+    grid_dep_wait();
     const size_t total = static_cast<size_t>(M) * N;
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -415,9 +419,21 @@ static cudaError_t run_tmem(const GemmRequest& r, const GemmArgs& args, cudaStre
         if (e != cudaSuccess) return e;
         attr_done.fetch_or(bit);
     }
-    const int grid = std::min(args.num_units, device_info(dev).sms);
-    k_fused_tmem<C><<<grid, C::NUM_THREADS, C::SMEM_ALLOC, st>>>(ta, tbm, args);
-    return cudaGetLastError();
+    // Programmatic stream serialisation: the kernel may start while the
+    // previous kernel in the stream is still running, if that kernel allows it
+    // (another narrow GEMM does, right after its set-up); it waits for that
+    // kernel before reading B and before storing D (k_fused_tmem).
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(std::min(args.num_units, device_info(dev).sms), 1, 1);
+    cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_fused_tmem<C>, ta, tbm, args);
 }
 
 template <int MODE, int FMT>
@@ -560,8 +576,17 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     if (e != cudaSuccess || splits <= 1) return e;
     const size_t total = static_cast<size_t>(r.M) * r.N;
     const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, static_cast<size_t>(sms) * 8));
-    k_splitk_reduce<<<std::max(blocks, 1), 256, 0, st>>>(a.ws, r.D, r.ldd, r.M, r.N, splits, r.alpha, r.out_f16);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(std::max(blocks, 1), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_splitk_reduce, static_cast<const float*>(a.ws), r.D, static_cast<long long>(r.ldd),
+                              r.M, r.N, splits, r.alpha, r.out_f16);
 }
 
 }  // namespace tb

@@ -225,6 +225,20 @@ __device__ __forceinline__ void mma_commit_pair(const uint64_t* bar, uint16_t ct
         : "memory");
 }
 
+// ---- programmatic dependent launch ---------------------------------------------------
+
+// Wait until the grids this one depends on (the previous kernel in the
+// stream, when this one was launched with programmatic stream serialisation)
+// have completed and their memory operations are visible.  Returns at once
+// otherwise.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Let the next kernel in the stream (if launched with programmatic stream
+// serialisation) be scheduled before this grid completes.
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- named (hardware) CTA barriers ---------------------------------------------------
 
 // Wait at named barrier `id` until `count` threads (a multiple of 32, whole

@@ -156,6 +156,84 @@ def test_fused_pair_tiles(tb, cuda, fmt, M, N, K):
         check(got[rows[0]:rows[1]], O.gemm(fmt, A, O.F16, B16, M, N, K, rows=rows, alpha=alpha))
 
 
+def test_narrow_chain_dependencies(tb, cuda):
+    """Back-to-back narrow GEMMs on one stream start before their predecessor
+    has finished (programmatic dependent launch) and stream their weights
+    early, but must wait for it before reading activations and before storing:
+    GEMM 2 reads GEMM 1's FP16 output as its activations, and GEMM 3 then
+    overwrites that buffer while GEMM 2 may still be streaming.  Each result
+    must equal, bit for bit, the same GEMM run alone."""
+    M1, N1, K1 = 1024, 64, 512        # D1: 1024 x 64 FP16 = B2 viewed as 16 x 4096
+    M2, N2, K2 = 2048, 16, 4096
+    A1, B1, al1 = make_operands(O.E4M3, M1, N1, K1, seed=31)
+    A2, _, al2 = make_operands(O.E2M1, M2, N2, K2, seed=32)
+    _, B3, _ = make_operands(O.E4M3, M1, N1, K1, seed=33)
+    dA1, dB1, dA2, dB3 = to_dev(cuda, A1), to_dev(cuda, B1), to_dev(cuda, A2), to_dev(cuda, B3)
+    X = empty_dev(cuda, M1 * N1 * 2)
+    D2 = empty_dev(cuda, M2 * N2 * 4)
+    F16 = tb.Out.F16
+
+    def g1(out):
+        tb.gemm_fused(O.E4M3, dA1, dB1, out, M1, N1, K1, out=F16, alpha=al1)
+
+    def g2(b, out):
+        tb.gemm_fused(O.E2M1, dA2, b, out, M2, N2, K2, alpha=al2)
+
+    def g3(out):
+        tb.gemm_fused(O.E4M3, dA1, dB3, out, M1, N1, K1, out=F16, alpha=al1)
+
+    # each GEMM alone
+    R1, R2, R3 = empty_dev(cuda, M1 * N1 * 2), empty_dev(cuda, M2 * N2 * 4), empty_dev(cuda, M1 * N1 * 2)
+    g1(R1); cuda.cuda.synchronize()
+    g2(R1, R2); cuda.cuda.synchronize()
+    g3(R3); cuda.cuda.synchronize()
+    want2, want3 = from_dev(R2, np.uint32), from_dev(R3, np.uint16)
+    check(want2.view(np.float32).reshape(M2, N2),
+          O.gemm(O.E2M1, A2, O.F16, from_dev(R1, np.uint16).reshape(N2, K2), M2, N2, K2, alpha=al2))
+    for _ in range(5):
+        X.fill_(0xA5)
+        D2.fill_(0xA5)
+        g1(X)
+        g2(X, D2)
+        g3(X)
+        cuda.cuda.synchronize()
+        np.testing.assert_array_equal(from_dev(D2, np.uint32), want2)
+        np.testing.assert_array_equal(from_dev(X, np.uint16), want3)
+
+
+def test_narrow_split_chain_shares_workspace(tb, cuda):
+    """Split-K narrow GEMMs back to back with one workspace: the second
+    GEMM's partials overwrite the workspace the first one's reduction reads,
+    and both the GEMM and the reduction start early (programmatic dependent
+    launch).  Each result must equal the same GEMM run alone, bit for bit."""
+    M, N, K = 1024, 16, 8192
+    A1, B1, al1 = make_operands(O.E4M3, M, N, K, seed=41)
+    A2, B2, al2 = make_operands(O.E4M3, M, N, K, seed=42)
+    ws_bytes = tb.fused_workspace_bytes(O.E4M3, M, N, K)
+    assert ws_bytes > 0
+    ws = empty_dev(cuda, ws_bytes)
+    dA1, dB1, dA2, dB2 = to_dev(cuda, A1), to_dev(cuda, B1), to_dev(cuda, A2), to_dev(cuda, B2)
+    D1, D2 = empty_dev(cuda, M * N * 4), empty_dev(cuda, M * N * 4)
+
+    def run(a, b, d, al):
+        tb.gemm_fused(O.E4M3, a, b, d, M, N, K, alpha=al, workspace=ws, workspace_bytes=ws_bytes)
+
+    run(dA1, dB1, D1, al1); cuda.cuda.synchronize()
+    want1 = from_dev(D1, np.uint32)
+    run(dA2, dB2, D2, al2); cuda.cuda.synchronize()
+    want2 = from_dev(D2, np.uint32)
+    check(want1.view(np.float32).reshape(M, N), O.gemm(O.E4M3, A1, O.F16, B1, M, N, K, alpha=al1))
+    for _ in range(5):
+        D1.fill_(0xA5)
+        D2.fill_(0xA5)
+        run(dA1, dB1, D1, al1)
+        run(dA2, dB2, D2, al2)
+        run(dA1, dB1, D1, al1)
+        cuda.cuda.synchronize()
+        np.testing.assert_array_equal(from_dev(D1, np.uint32), want1)
+        np.testing.assert_array_equal(from_dev(D2, np.uint32), want2)
+
+
 def kernels_launched(cuda, fn):
     """Names of the kernels `fn` launches (CUPTI trace through torch.profiler)."""
     from torch.profiler import ProfilerActivity, profile
