@@ -156,7 +156,14 @@ tb_status tb_gemm_f16(const uint16_t* A, const uint16_t* B, void* D, int M, int 
  * gemm_fp8_fused_fp16 (src/gemm_fused.cu:24-49) quantizes both operands, see
  * tb_gemm_fp8_fused_fp16 for that one.
  * `workspace` (device, may be NULL when tb_gemm_fused_workspace returns 0)
- * holds split-K partial sums for short-and-wide shapes. */
+ * holds split-K partial sums for short-and-wide shapes.
+ * Few-token shapes (N <= 64; N <= 128 for the one-byte and FP4 formats)
+ * run a kernel launched with programmatic dependent launch: it may start
+ * while the previous kernel on `stream` runs, if that kernel allows it (the
+ * same kernel and its split-K reduction do), and then reads one-byte and FP4
+ * weights before that kernel has finished; B, D, the workspace and BF16/TF32
+ * weights are accessed only after it has.  Do not have a kernel that
+ * triggers its dependents early write the weights of a following call. */
 tb_status tb_gemm_fused(tb_format a_fmt, const void* A, const uint16_t* B, void* D,
                         int M, int N, int K, tb_out_type out, float alpha,
                         void* workspace, size_t workspace_bytes, tb_stream_t stream);
