@@ -94,6 +94,20 @@ struct FusedPairCfg {
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
+// Pair tile u -> (tile row, tile column).  The operand that every wave of
+// clusters reads whole stays in L2 across waves: with M tiles varying fastest
+// a wave covers all rows of A and a few B columns, so A should be the smaller
+// operand; otherwise N tiles vary fastest (GemmArgs::n_fastest).
+__device__ __forceinline__ void pair_tile(const GemmArgs& p, int u, int tiles_m, int tiles_n, int& tm, int& tn) {
+    if (p.n_fastest) {
+        tm = u / tiles_n;
+        tn = u % tiles_n;
+    } else {
+        tm = u % tiles_m;
+        tn = u / tiles_m;
+    }
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     k_fused_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs p) {
@@ -159,7 +173,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         uint32_t ph = 0;
         bool ok = true;
         for (int u = cid; ok && u < units; u += ncl) {
-            const int tn = u / tiles_m;
+            int tm, tn;
+            pair_tile(p, u, tiles_m, tiles_n, tm, tn);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
                 if (elect_one()) {
@@ -225,7 +240,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         const int quarter = warp & 3;
         int t = 0;
         for (int u = cid; u < units; u += ncl, ++t) {
-            const int tm = u % tiles_m, tn = u / tiles_m;
+            int tm, tn;
+            pair_tile(p, u, tiles_m, tiles_n, tm, tn);
             const bool ok = mbar_wait(acc_full, t & 1, abort_flag);
             if (!__all_sync(0xFFFFFFFFu, ok)) break;
             tc_fence_after();
@@ -253,7 +269,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         long long issued = 0;
         bool ok = true;
         for (int u = cid; ok && u < units; u += ncl) {
-            const int tm = u % tiles_m;
+            int tm, tn;
+            pair_tile(p, u, tiles_m, tiles_n, tm, tn);
             for (int kb = 0; kb < p.num_kb; kb += C::RK) {
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&a_empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
                 if (elect_one()) {

@@ -171,6 +171,7 @@ struct GemmArgs {
     long long ldd;
     int out_f16;     // 1: FP16 output, 0: FP32
     int vec_ok;      // 1: D rows allow 16-byte vector stores
+    int n_fastest;   // fused pair kernel: tile order with N tiles varying fastest
     int out_i32;     // 1: D is INT32 (kind::i8), stored as accumulated, no alpha
     float* ws;       // split-K partials [splits][M][N] (FP32), when splits > 1
     uint32_t idesc_ab;  // native mode: A/B format fields of the instruction descriptor
