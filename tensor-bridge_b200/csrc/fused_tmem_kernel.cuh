@@ -97,6 +97,7 @@ struct TmemCfg {
     static constexpr bool SYNCW = SR >= 2 * SPR;
     // Named barriers (0 is __syncthreads): START 1-2, DONE 3-4.
     static constexpr uint32_t NB_START = 1, NB_DONE = 3, NB_COUNT = (ND + 1) * 32;
+    static constexpr uint32_t NB_SETUP = 5;  // set-up: warp 0 arrives, the others wait
 
     static constexpr int A_COL0 = 2 * BN > 128 ? 2 * BN : 128;
     static constexpr int TMEM_COLS = 512;
@@ -289,6 +290,10 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         mbar_init(fin_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
+        // The next narrow GEMM in the stream may start now: its weight stream
+        // then overlaps this kernel's tail (launched with programmatic stream
+        // serialisation; see the dependency waits below).
+        grid_dep_launch_dependents();
     }
     if (warp == 0 && lane == 0) tma_prefetch_desc(&tmA);
     if (warp == C::B_WARP && lane == 0) tma_prefetch_desc(&tmB);
@@ -296,14 +301,19 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         tmem_alloc(tmem_holder, C::TMEM_COLS);
         tmem_relinquish();
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_holder;
-    // The next narrow GEMM in the stream may start now: its weight stream then
-    // overlaps this kernel's tail (launched with programmatic stream
-    // serialisation; see the dependency waits below).
-    if (threadIdx.x == 0) grid_dep_launch_dependents();
+    // Set-up barrier: the raw-A producer (warp 0, whose thread 0 initialised
+    // the mbarriers) only arrives and starts streaming at once; the other
+    // warps also need the TMEM allocation and wait for everyone.
+    uint32_t tmem_base = 0;
+    if (warp == 0) {
+        __syncwarp();
+        named_bar_arrive(C::NB_SETUP, C::NUM_THREADS);
+    } else {
+        tc_fence_before();
+        named_bar_sync(C::NB_SETUP, C::NUM_THREADS);
+        tc_fence_after();
+        tmem_base = *tmem_holder;
+    }
 
     if (warp == 0) {
         // ---------------- TMA producer: raw A stages ----------------

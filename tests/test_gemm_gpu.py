@@ -56,6 +56,7 @@ def check(got, want, tol=TOL):
 
 
 SHAPES = [
+    (2500, 2000, 128),   # pair tiles with ragged M and N
     (256, 256, 256),     # the 256^3 configuration
     (128, 256, 64),      # one tile, one k-block
     (200, 72, 48),       # ragged M/N, K not a multiple of 64
@@ -318,7 +319,8 @@ NATIVE_PAIRS = [(O.E2M1_HW, O.E2M1_HW), (O.E4M3, O.E2M1_HW), (O.E2M1_HW, O.E4M3)
 
 
 @pytest.mark.parametrize("fa,fb", NATIVE_PAIRS)
-@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (384, 200, 640), (128, 16, 2048), (1000, 72, 96)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (384, 200, 640), (128, 16, 2048), (1000, 72, 96),
+                                   (2500, 2000, 128)])  # pair tiles, ragged M and N
 def test_gemm_native_formats(tb, cuda, fa, fb, M, N, K):
     """qA @ qB on kind::f8f6f4 for FP4 (16U4_ALIGN16B TMA expansion), E5M2
     and mixed pairs, each operand with its own per-tensor scale."""

@@ -51,7 +51,7 @@ def test_decode_transposed(tb, cuda, rows, cols):
 
 
 SHAPES = [(256, 256, 256), (128, 256, 128), (200, 72, 48), (384, 520, 320), (1000, 16, 4096), (128, 1, 2048),
-          (300, 100, 1056), (4096, 512, 512)]
+          (300, 100, 1056), (4096, 512, 512), (2500, 2000, 128)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
