@@ -438,7 +438,9 @@ def mlp_weight_only(torch, tb, peaks, iters: int = 20):
     against decode kernel + GEMM.  Each figure is per launch of a back-to-back
     sequence over C copies of the weight (C x stored bytes > 400 MB, so every
     launch streams its weight from HBM) inside a CUDA graph, median of 20
-    replays.  Algorithmic bytes = stored W + X + D."""
+    replays; the few-token fused kernels of the sequence overlap their
+    successor's start through programmatic dependent launch, as consecutive
+    layers would.  Algorithmic bytes = stored W + X + D."""
     out = []
     for (M, K) in ((14336, 4096), (4096, 14336)):
         for fname, fmt in (("e4m3", tb.Format.E4M3), ("e2m1", tb.Format.E2M1)):
