@@ -193,31 +193,53 @@ __global__ void __launch_bounds__(256) k_decode_e4m3_i8(const uint4* __restrict_
 }
 
 // src [rows x cols] -> dst [cols x rows] (the reference's B8[col * K + k]),
-// through a 64-row x 32-column shared-memory tile as k_decode_transposed.
+// through a 64 x 64-byte shared-memory tile: each thread reads 16 codes of a
+// source row (one 16-byte load when the tile lies inside the matrix and rows
+// are 16-byte aligned), converts them, scatters the bytes into the transposed
+// tile, and then writes 16 bytes of one output row.  Edge tiles take bytes one
+// at a time.
 __global__ void __launch_bounds__(256) k_decode_e4m3_i8_transposed(const uint8_t* __restrict__ src,
                                                                    uint8_t* __restrict__ dst, int rows, int cols,
                                                                    float scale) {
-    __shared__ uint8_t tile[32][64 + 4];
-    const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    constexpr int PITCH = 80;  // 64 bytes + 16: keeps 16-byte alignment of tile rows
+    __shared__ __align__(16) uint8_t tile[64 * PITCH];
+    const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 64;
+    const int t = threadIdx.x;
+    const bool whole = r0 + 64 <= rows && c0 + 64 <= cols;
+    {
+        const int lr = t >> 2, v = t & 3;  // source row r0 + lr, columns c0 + 16 v ..
+        const int r = r0 + lr, c = c0 + 16 * v;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        const uint8_t* in = src + static_cast<size_t>(r) * cols + c;
+        if (whole && (cols & 15) == 0 && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
+            const uint4 q = *reinterpret_cast<const uint4*>(in);
+            w[0] = e4m3x4_to_i8x4(q.x, scale);
+            w[1] = e4m3x4_to_i8x4(q.y, scale);
+            w[2] = e4m3x4_to_i8x4(q.z, scale);
+            w[3] = e4m3x4_to_i8x4(q.w, scale);
+        } else if (r < rows) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const int r = r0 + ty + 8 * k, c = c0 + tx;
-        if (r < rows && c < cols)
-            tile[tx][ty + 8 * k] = static_cast<uint8_t>(
-                e4m3_to_i8_byte(tensor_bridge::e4m3_to_half_bits(src[static_cast<size_t>(r) * cols + c]), scale));
+            for (int j = 0; j < 16; ++j)
+                if (c + j < cols)
+                    w[j >> 2] |= e4m3_to_i8_byte(tensor_bridge::e4m3_to_half_bits(in[j]), scale) << (8 * (j & 3));
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) tile[(16 * v + j) * PITCH + lr] = static_cast<uint8_t>(w[j >> 2] >> (8 * (j & 3)));
     }
     __syncthreads();
-    // Each warp writes 64 consecutive bytes of an output row, two per lane.
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int oc = ty + 8 * k;
-        const int c = c0 + oc;
-        const int r = r0 + 2 * tx;
+    {
+        const int oc = t >> 2, v = t & 3;  // output row c0 + oc, its bytes r0 + 16 v ..
+        const int c = c0 + oc, r = r0 + 16 * v;
         if (c < cols) {
             uint8_t* out = dst + static_cast<size_t>(c) * rows + r;
-            if (r < rows) out[0] = tile[oc][2 * tx];
-            if (r + 1 < rows) out[1] = tile[oc][2 * tx + 1];
+            const uint8_t* row = tile + oc * PITCH + 16 * v;
+            if (whole && (rows & 15) == 0 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+                *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(row);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (r + j < rows) out[j] = row[j];
+            }
         }
     }
 }
@@ -329,7 +351,7 @@ cudaError_t decode_e4m3_i8_launch(const uint8_t* src, int8_t* dst, size_t n, flo
 
 cudaError_t decode_e4m3_i8_transposed_launch(const uint8_t* src, int8_t* dst, int rows, int cols, float scale,
                                              cudaStream_t st) {
-    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
+    dim3 grid((cols + 63) / 64, (rows + 63) / 64);
     k_decode_e4m3_i8_transposed<<<grid, 256, 0, st>>>(src, reinterpret_cast<uint8_t*>(dst), rows, cols, scale);
     return cudaGetLastError();
 }

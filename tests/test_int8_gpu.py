@@ -38,7 +38,7 @@ def test_decode_tails_and_misalignment(tb, cuda, n, off):
     assert np.all(got[:off].view(np.uint8) == 0xA5), "wrote before the destination"
 
 
-@pytest.mark.parametrize("rows,cols", [(64, 32), (100, 33), (4096, 16), (7, 300)])
+@pytest.mark.parametrize("rows,cols", [(64, 32), (100, 33), (4096, 16), (7, 300), (256, 192), (192, 130), (1024, 1024)])
 def test_decode_transposed(tb, cuda, rows, cols):
     rng = np.random.default_rng(rows * cols)
     src = rng.integers(0, 256, size=(rows, cols), dtype=np.uint8)
