@@ -143,6 +143,89 @@ __global__ void __launch_bounds__(256) k_decode_transposed(const void* __restric
     }
 }
 
+// 16 consecutive stored values at `p` (16-byte aligned) -> 16 FP16 values,
+// two per word, first value in the low half.
+template <int FMT>
+__device__ __forceinline__ void decode16_vec(const uint8_t* p, uint32_t (&h)[8]) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+    if constexpr (FMT == kBF16) {
+        const uint4 a = q[0], b = q[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) h[k] = decode_bf16_x2(w[k]);
+    } else if constexpr (FMT == kTF32) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 a = q[k];
+            h[2 * k] = decode_tf32_x2(a.x, a.y);
+            h[2 * k + 1] = decode_tf32_x2(a.z, a.w);
+        }
+    } else {
+        const uint4 a = q[0];
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if constexpr (FMT == kE4M3) decode_e4m3_x4(w[k], h[2 * k], h[2 * k + 1]);
+            else if constexpr (FMT == kE5M2) decode_e5m2_x4(w[k], h[2 * k], h[2 * k + 1]);
+            else decode_e2m1_unpacked_x4(w[k], h[2 * k], h[2 * k + 1]);
+        }
+    }
+}
+
+// Formats of one value per 1, 2 or 4 bytes (E4M3, E5M2, unpacked E2M1, BF16,
+// TF32): 64 x 64-value tiles, each thread reading 16 values of a source row
+// with 16-byte loads (whole tiles, 16-byte aligned rows), converting them,
+// and scattering the FP16 values into the transposed shared-memory tile; each
+// thread then writes 16 values (32 bytes) of one output row.  Edge tiles go
+// element by element.
+template <int FMT>
+__global__ void __launch_bounds__(256) k_decode_transposed_vec(const uint8_t* __restrict__ src,
+                                                               uint16_t* __restrict__ dst, int rows, int cols) {
+    constexpr int VB = FMT == kBF16 ? 2 : FMT == kTF32 ? 4 : 1;  // bytes per stored value
+    constexpr int PITCH = 72;  // halves per tile row: 64 + 8 keeps rows 16-byte aligned
+    __shared__ __align__(16) uint16_t tile[64 * PITCH];
+    const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 64;
+    const int t = threadIdx.x;
+    const bool whole = r0 + 64 <= rows && c0 + 64 <= cols;
+    {
+        const int lr = t >> 2, v = t & 3;  // source row r0 + lr, columns c0 + 16 v ..
+        const int r = r0 + lr, c = c0 + 16 * v;
+        uint32_t h[8];
+        if (whole && ((cols * VB) & 15) == 0 && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
+            decode16_vec<FMT>(src + (static_cast<size_t>(r) * cols + c) * VB, h);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int ca = c + 2 * k;
+                const uint32_t lo = (r < rows && ca < cols) ? decode_at<FMT>(src, static_cast<size_t>(r) * cols + ca) : 0u;
+                const uint32_t hi =
+                    (r < rows && ca + 1 < cols) ? decode_at<FMT>(src, static_cast<size_t>(r) * cols + ca + 1) : 0u;
+                h[k] = lo | (hi << 16);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            tile[(16 * v + j) * PITCH + lr] = static_cast<uint16_t>(h[j >> 1] >> (16 * (j & 1)));
+    }
+    __syncthreads();
+    {
+        const int oc = t >> 2, v = t & 3;  // output row c0 + oc, its values r0 + 16 v ..
+        const int c = c0 + oc, r = r0 + 16 * v;
+        if (c < cols) {
+            uint16_t* out = dst + static_cast<size_t>(c) * rows + r;
+            const uint16_t* row = tile + oc * PITCH + 16 * v;
+            if (whole && (rows & 7) == 0 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+                reinterpret_cast<uint4*>(out)[0] = reinterpret_cast<const uint4*>(row)[0];
+                reinterpret_cast<uint4*>(out)[1] = reinterpret_cast<const uint4*>(row)[1];
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (r + j < rows) out[j] = row[j];
+            }
+        }
+    }
+}
+
 // ---- FP8 E4M3 -> INT8 (the reference's integer tensor-core path) ----------------
 
 // One E4M3 code -> INT8 as src/gemm.cu:35-41 computes it:
@@ -303,8 +386,13 @@ static cudaError_t launch_decode(const void* src, uint16_t* dst, size_t n, cudaS
 
 template <int FMT>
 static cudaError_t launch_decode_t(const void* src, uint16_t* dst, int rows, int cols, cudaStream_t st) {
-    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
-    k_decode_transposed<FMT><<<grid, 256, 0, st>>>(src, dst, rows, cols);
+    if constexpr (FMT == kE4M3 || FMT == kE5M2 || FMT == kE2M1U || FMT == kBF16 || FMT == kTF32) {
+        dim3 grid((cols + 63) / 64, (rows + 63) / 64);
+        k_decode_transposed_vec<FMT><<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(src), dst, rows, cols);
+    } else {
+        dim3 grid((cols + 31) / 32, (rows + 63) / 64);
+        k_decode_transposed<FMT><<<grid, 256, 0, st>>>(src, dst, rows, cols);
+    }
     return cudaGetLastError();
 }
 

@@ -80,7 +80,7 @@ def test_decode_large(tb, cuda, fmt):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("rows,cols", [(1, 2), (64, 32), (96, 80), (37, 130), (300, 258)])
+@pytest.mark.parametrize("rows,cols", [(1, 2), (64, 32), (96, 80), (37, 130), (300, 258), (256, 192), (1024, 1024)])
 def test_decode_transposed(tb, cuda, fmt, rows, cols):
     rng = np.random.default_rng(rows * 1000 + cols)
     n = rows * cols
