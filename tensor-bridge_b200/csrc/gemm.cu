@@ -272,20 +272,27 @@ static cudaError_t run_pair(const GemmRequest& r, const GemmArgs& args, int clus
     CUtensorMap ta, tbm;
     const uint64_t K = static_cast<uint64_t>(r.K);
     bool ok;
+    // B in 64-row boxes: one per CTA for a half tile, two for a whole one.
     if constexpr (MODE == kModeF16) {
         ok = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.A, K, r.M, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
-             make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+             make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT16, r.B, K, r.N, K * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     } else if constexpr (MODE == kModeNative8) {
-        ok = make_native_map(&ta, r.a_fmt, r.A, K, r.M, 128) && make_native_map(&tbm, r.b_fmt, r.B, K, r.N, 128);
+        ok = make_native_map(&ta, r.a_fmt, r.A, K, r.M, 128) && make_native_map(&tbm, r.b_fmt, r.B, K, r.N, 64);
     } else {
-        ok = make_native_map(&ta, kE4M3, r.A, K, r.M, 128) && make_native_map(&tbm, kE4M3, r.B, K, r.N, 128);
+        ok = make_native_map(&ta, kE4M3, r.A, K, r.M, 128) && make_native_map(&tbm, kE4M3, r.B, K, r.N, 64);
     }
     if (!ok) {
         *why = "cuTensorMapEncodeTiled rejected the operand layout";
         return cudaErrorInvalidValue;
     }
-    const int units = ((r.M + C::BM - 1) / C::BM) * ((r.N + C::BN - 1) / C::BN);
-    return launch_pairs<C>(k_gemm_pair<C>, ta, tbm, args, units, clusters, st);
+    // Whole tiles for the full waves; the R tiles of a partial last wave as 2R
+    // halves when those fit in one wave (the last wave then takes half a tile).
+    const int tiles = ((r.M + C::BM - 1) / C::BM) * ((r.N + C::BN - 1) / C::BN);
+    const int rem = tiles % clusters;
+    GemmArgs a = args;
+    a.pair_full = (rem > 0 && 2 * rem <= clusters) ? tiles - rem : tiles;
+    const int units = a.pair_full + 2 * (tiles - a.pair_full);
+    return launch_pairs<C>(k_gemm_pair<C>, ta, tbm, a, units, clusters, st);
 }
 
 // Fused decode + GEMM on 256 x 512 SM-pair tiles (fused_pair_kernel.cuh):
@@ -525,7 +532,11 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
                 return r.kind == GemmKind::kF16 ? 128u : (f == kE2M1HW ? 64u : 128u);
             };
             a.tx_bytes = 128u * row_bytes(r.a_fmt) + 128u * row_bytes(r.kind == GemmKind::kNative ? r.b_fmt : r.a_fmt);
-            if (r.kind == GemmKind::kInt8) a.tx_bytes = 2u * 128u * 128u;
+            a.tx_b_half = 64u * row_bytes(r.kind == GemmKind::kNative ? r.b_fmt : r.a_fmt);
+            if (r.kind == GemmKind::kInt8) {
+                a.tx_bytes = 2u * 128u * 128u;
+                a.tx_b_half = 64u * 128u;
+            }
             if (r.kind != GemmKind::kNative) a.idesc_ab = 0;
             cudaError_t e2 = mode == kModeF16 ? run_pair<kModeF16>(r, a, clusters, st, why)
                              : mode == kModeNative8 ? run_pair<kModeNative8>(r, a, clusters, st, why)

@@ -176,6 +176,11 @@ struct GemmArgs {
     float* ws;       // split-K partials [splits][M][N] (FP32), when splits > 1
     uint32_t idesc_ab;  // native mode: A/B format fields of the instruction descriptor
     uint32_t tx_bytes;  // native mode: TMA bytes per operand stage (packed FP4 counts 64 per 128-value row)
+    // Pair GEMM (k_gemm_pair): work units [0, pair_full) are whole 256 x 256
+    // tiles; the tiles after them (the last, partial wave) run as two
+    // 256 x 128 halves each.  tx_b_half: TMA bytes of 64 B rows.
+    int pair_full;
+    uint32_t tx_b_half;
 };
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) ----------------------

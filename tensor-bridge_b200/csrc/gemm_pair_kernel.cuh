@@ -4,7 +4,8 @@
 //
 //   D[M x N] = alpha * A[M x K] * B[N x K]^T      (INT8: exact INT32 D)
 //
-// A cluster of two CTAs owns a 256 x 256 output tile.  Each CTA stages its own
+// A cluster of two CTAs owns a 256 x 256 output tile (or, for the tiles of a
+// partial last wave, a 256 x 128 half of one; see pair_unit).  Each CTA stages its own
 // 128 rows of A and its own 128 rows of B (half of the tile's N) in its shared
 // memory; one elected thread of the leader CTA (rank 0) issues
 // tcgen05.mma.cta_group::2 with M = 256, which reads both CTAs' halves and
@@ -57,8 +58,29 @@ struct PairCfg {
     static constexpr int TMEM_COLS = 512;
     static constexpr int KIND = MODE == kModeF16 ? 0 : MODE == kModeNative8 ? 1 : 2;
     static constexpr uint32_t IDESC = MODE == kModeInt8 ? idesc_i8(BM, BN) : idesc_make(0u, 0u, BM, BN);
+    // Half tiles (256 x 128) of the last wave.
+    static constexpr uint32_t IDESC_HALF =
+        MODE == kModeInt8 ? idesc_i8(BM, BN / 2) : idesc_make(0u, 0u, BM, BN / 2);
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
+
+// Work unit u -> tile row, first column and width.  The tiles that would form
+// a partial last wave are split into two 256 x 128 halves: the last wave then
+// takes half a tile's time (4096^2: 222 whole tiles and 68 halves on 74
+// clusters, 3.5 tile times instead of 4).  The split is along N only, so every
+// output element is still one accumulation over all of K in the same order.
+__device__ __forceinline__ void pair_unit(const GemmArgs& p, int u, int tiles_m, int& tm, int& col0, bool& half) {
+    int tile, h = 0;
+    half = u >= p.pair_full;
+    if (half) {
+        tile = p.pair_full + ((u - p.pair_full) >> 1);
+        h = (u - p.pair_full) & 1;
+    } else {
+        tile = u;
+    }
+    tm = tile % tiles_m;
+    col0 = (tile / tiles_m) * 256 + h * 128;
+}
 
 template <class C>
 __global__ void __launch_bounds__(C::NUM_THREADS, 1)
@@ -112,7 +134,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
 
     const int tiles_m = (p.M + C::BM - 1) / C::BM;
     const int tiles_n = (p.N + C::BN - 1) / C::BN;
-    const int units = tiles_m * tiles_n;
+    const int units = p.pair_full + 2 * (tiles_m * tiles_n - p.pair_full);
     const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
 
     if (warp == 0) {
@@ -121,16 +143,22 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         uint32_t ph = 0;
         bool ok = true;
         for (int u = cid; ok && u < units; u += ncl) {
-            const int tm = u % tiles_m, tn = u / tiles_m;
+            int tm, col0;
+            bool half;
+            pair_unit(p, u, tiles_m, tm, col0, half);
+            // This CTA's B rows: 128 of a whole tile, 64 of a half (64-row boxes).
+            const int brows = half ? 64 : 128;
+            const uint32_t tx = half ? p.tx_bytes - p.tx_b_half : p.tx_bytes;
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
                 if (elect_one()) {
-                    if (leader) mbar_arrive_expect_tx(&full[s], 2u * p.tx_bytes);
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2u * tx);
                     const uint32_t fb = leader_bar(&full[s]);
                     uint8_t* st = smem + s * C::STAGE_BYTES;
                     tma_load_2d_pair(st, &tmA, fb, kb * C::KB_ELEMS, tm * C::BM + static_cast<int>(rank) * 128);
-                    tma_load_2d_pair(st + C::A_BYTES, &tmB, fb, kb * C::KB_ELEMS,
-                                     tn * C::BN + static_cast<int>(rank) * 128);
+                    const int b0 = col0 + static_cast<int>(rank) * brows;
+                    tma_load_2d_pair(st + C::A_BYTES, &tmB, fb, kb * C::KB_ELEMS, b0);
+                    if (!half) tma_load_2d_pair(st + C::A_BYTES + 8192, &tmB, fb, kb * C::KB_ELEMS, b0 + 64);
                 }
                 __syncwarp();
                 if (++s == C::S) { s = 0; ph ^= 1u; }
@@ -145,6 +173,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             int t = 0;
             bool ok = true;
             for (int u = cid; ok && u < units; u += ncl, ++t) {
+                const uint32_t idesc = (u >= p.pair_full ? C::IDESC_HALF : C::IDESC) | p.idesc_ab;
                 const int acc = t & 1;
                 const uint32_t aph = (t >> 1) & 1;
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag))) { ok = false; break; }
@@ -159,8 +188,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
                             const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
-                            mma_pair<C::KIND>(d_tmem, sdesc_make(a_lo + 2u * kk), sdesc_make(b_lo + 2u * kk),
-                                              C::IDESC | p.idesc_ab, accum);
+                            mma_pair<C::KIND>(d_tmem, sdesc_make(a_lo + 2u * kk), sdesc_make(b_lo + 2u * kk), idesc,
+                                              accum);
                         }
                         mma_commit_pair(&empty[s], 0x3);
                     }
@@ -181,7 +210,10 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
         int t = 0;
         for (int u = cid; u < units; u += ncl, ++t) {
-            const int tm = u % tiles_m, tn = u / tiles_m;
+            int tm, col0;
+            bool half;
+            pair_unit(p, u, tiles_m, tm, col0, half);
+            const int ncols = half ? C::BN / 2 : C::BN;
             const int acc = t & 1;
             const uint32_t aph = (t >> 1) & 1;
             const bool ok = mbar_wait(&acc_full[acc], aph, abort_flag);
@@ -191,11 +223,11 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             const uint32_t t_row =
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * C::BN);
 #pragma unroll 1
-            for (int c = 0; c < C::BN; c += 32) {
+            for (int c = 0; c < ncols; c += 32) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(t_row + c, v);
                 tmem_wait_ld();
-                store_row_chunk<32>(p, 0, row, tn * C::BN + c, v);
+                store_row_chunk<32>(p, 0, row, col0 + c, v);
             }
             tc_fence_before();
             __syncwarp();
