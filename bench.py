@@ -81,8 +81,9 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, cuda_index: int):
+    def __init__(self, cuda_index: int, interval_ms: int = 100):
         # nvidia-smi numbers GPUs physically; map through CUDA_VISIBLE_DEVICES.
+        self.interval_ms = interval_ms
         vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
         self.gpu = vis[cuda_index].strip() if cuda_index < len(vis) else str(cuda_index)
         self.proc = None
@@ -92,7 +93,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                          "-i", str(self.gpu), "-lms", str(self.interval_ms)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -114,7 +115,7 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], [], set()
+        sm, smax, watts, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
@@ -125,13 +126,17 @@ class ClockSampler:
                 smax.append(float(parts[2]))
             except ValueError:
                 continue
+            try:
+                watts.append(float(parts[3]))
+            except ValueError:
+                pass
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "power_w": statistics.median(watts) if watts else None, "reasons": sorted(reasons)}
 
 
 # ---- distributed plumbing ------------------------------------------------------------------
@@ -524,21 +529,26 @@ def int8_square(torch, tb, n: int = 4096, iters: int = 10):
             "fp8_fused_int8_tops": ops / ms_f / 1e9}
 
 
-def fp4_square(torch, tb, peaks, n: int = 8192, iters: int = 10):
+def fp4_square(torch, tb, peaks, n: int = 8192, iters: int = 40):
     """Large square fused GEMM: A packed E2M1 from N(0, 1) with scale 6/maxabs,
-    B FP16 N(0, 1), FP32 accumulation, FP16 output."""
+    B FP16 N(0, 1), FP32 accumulation, FP16 output.  The SM clocks and power
+    are sampled every 10 ms over this section alone ("clocks"): a GEMM at this
+    rate runs into the 1 kW power cap, which lowers the clock."""
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
     A, alpha = weights_q(torch, tb, tb.Format.E2M1, n, n, 1.0, seed=8192)
     g = torch.Generator(device="cuda")
     g.manual_seed(8193)
     B = torch.randn(n, n, generator=g, device="cuda").half()
     D = torch.empty(n, n, dtype=torch.float16, device="cuda")
+    clocks = ClockSampler(torch.cuda.current_device(), interval_ms=10)
+    clocks.start()
     ms = time_each(torch, lambda: tb.gemm_fused(tb.Format.E2M1, A, B, D, n, n, n, out=tb.Out.F16, alpha=alpha),
                    iters, flush)
+    clk = clocks.stop()
     tf = 2.0 * n ** 3 / ms / 1e9
     return {"M": n, "N": n, "K": n, "fmt": "e2m1 packed", "out": "f16", "ms": ms, "tflops": tf,
             "pct_f16_dense_peak_nominal": 100 * tf / 2250.0,
-            "frac_of_measured_bf16": tf / peaks["bf16_tflops"]}
+            "frac_of_measured_bf16": tf / peaks["bf16_tflops"], "clocks": clk}
 
 
 def sharded_weight_gemm(torch, tb, dist, steps: int = 5, warmup: int = 2):
