@@ -21,10 +21,10 @@ namespace tb {
 // the 32 lanes of a warp touch 32 consecutive items, so both the loads and the
 // stores of a warp are contiguous (no half-written 32-byte sectors).
 template <int FMT> struct Item;
-template <> struct Item<kE4M3> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
-template <> struct Item<kE5M2> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
-template <> struct Item<kE2M1U> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
-template <> struct Item<kE2M1> { using In = uint32_t; using Out = uint4; static constexpr int kElems = 8, kRep = 8; };
+template <> struct Item<kE4M3> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 16; };
+template <> struct Item<kE5M2> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 16; };
+template <> struct Item<kE2M1U> { using In = uint2; using Out = uint4; static constexpr int kElems = 8, kRep = 16; };
+template <> struct Item<kE2M1> { using In = uint32_t; using Out = uint4; static constexpr int kElems = 8, kRep = 16; };
 template <> struct Item<kBF16> { using In = uint4; using Out = uint4; static constexpr int kElems = 8, kRep = 4; };
 template <> struct Item<kTF32> { using In = uint4; using Out = uint2; static constexpr int kElems = 4, kRep = 4; };
 template <> struct Item<kF16> { using In = uint4; using Out = uint4; static constexpr int kElems = 8, kRep = 4; };
@@ -68,7 +68,10 @@ __device__ __forceinline__ uint16_t decode_at(const void* src, size_t i) {
 
 // Grid-stride over warp chunks of 32 x kRep consecutive items.  Each thread
 // issues its kRep loads (lane, lane + 32, ...) before any decode, then stores
-// the kRep outputs; the last partial chunk is bounds-checked per item.
+// the kRep outputs with streaming (evict-first) stores -- the outputs are not
+// re-read from L2 by this kernel; the last partial chunk is bounds-checked
+// per item.  (16 one-byte or FP4 items in flight per thread and the streaming
+// stores: 14336 x 4096 E4M3 5.55 -> 5.99 TB/s, E2M1 5.23 -> 5.80 TB/s.)
 template <int FMT>
 __global__ void __launch_bounds__(256) k_decode_stream(const typename Item<FMT>::In* __restrict__ src,
                                                        typename Item<FMT>::Out* __restrict__ dst, size_t items,
@@ -86,7 +89,7 @@ __global__ void __launch_bounds__(256) k_decode_stream(const typename Item<FMT>:
 #pragma unroll
             for (int j = 0; j < I::kRep; ++j) in[j] = __ldcs(src + base + j * 32 + lane);
 #pragma unroll
-            for (int j = 0; j < I::kRep; ++j) dst[base + j * 32 + lane] = decode_item<FMT>(in[j]);
+            for (int j = 0; j < I::kRep; ++j) __stcs(dst + base + j * 32 + lane, decode_item<FMT>(in[j]));
         } else {
 #pragma unroll
             for (int j = 0; j < I::kRep; ++j)

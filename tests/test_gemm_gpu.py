@@ -202,6 +202,34 @@ def test_narrow_chain_dependencies(tb, cuda):
         np.testing.assert_array_equal(from_dev(X, np.uint16), want3)
 
 
+def test_narrow_chain_tf32_weights_from_previous_output(tb, cuda):
+    """A narrow GEMM with TF32 weights that are the previous narrow GEMM's FP32
+    output: its raw-weight stream must wait for that GEMM (BF16 and TF32
+    weights are read only after the dependency wait)."""
+    M1, N1, K1 = 1024, 64, 512      # D1: 1024 x 64 FP32 = A2 viewed as 128 x 512 TF32 words
+    M2, N2, K2 = 128, 16, 512
+    A1, B1, al1 = make_operands(O.E4M3, M1, N1, K1, seed=51)
+    _, B2, _ = make_operands(O.E4M3, M2, N2, K2, seed=52)
+    dA1, dB1, dB2 = to_dev(cuda, A1), to_dev(cuda, B1), to_dev(cuda, B2)
+    X = empty_dev(cuda, M1 * N1 * 4)
+    R = empty_dev(cuda, M1 * N1 * 4)
+    D2, W2 = empty_dev(cuda, M2 * N2 * 4), empty_dev(cuda, M2 * N2 * 4)
+    tb.gemm_fused(O.E4M3, dA1, dB1, R, M1, N1, K1, alpha=al1)
+    cuda.cuda.synchronize()
+    tb.gemm_fused(O.TF32, R, dB2, W2, M2, N2, K2)
+    cuda.cuda.synchronize()
+    want = from_dev(W2, np.uint32)
+    check(want.view(np.float32).reshape(M2, N2),
+          O.gemm(O.TF32, from_dev(R, np.uint32).reshape(M2, K2), O.F16, B2, M2, N2, K2))
+    for _ in range(5):
+        X.fill_(0xA5)
+        D2.fill_(0xA5)
+        tb.gemm_fused(O.E4M3, dA1, dB1, X, M1, N1, K1, alpha=al1)
+        tb.gemm_fused(O.TF32, X, dB2, D2, M2, N2, K2)
+        cuda.cuda.synchronize()
+        np.testing.assert_array_equal(from_dev(D2, np.uint32), want)
+
+
 def test_narrow_split_chain_shares_workspace(tb, cuda):
     """Split-K narrow GEMMs back to back with one workspace: the second
     GEMM's partials overwrite the workspace the first one's reduction reads,
