@@ -324,6 +324,9 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         // BF16 and TF32 words could be an earlier GEMM's FP16 / FP32 output:
         // wait for it first.
         if constexpr (C::FMT == kBF16 || C::FMT == kTF32) grid_dep_wait();
+        // Each weight byte is read once: evict-first in L2, which keeps the
+        // activations (read by every CTA) resident.
+        const uint64_t wpol = l2_policy_evict_first();
         uint32_t st = 0;  // CTA-wide stage number
         bool ok = true;
         NCursor cur;
@@ -354,8 +357,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                         const int x0 = (kb + pos * C::RSK) * raw_elems_per_kblock(C::FMT);
 #pragma unroll
                         for (int b = 0; b < C::NBOX; ++b)
-                            tma_load_2d(dst + b * 16384, &tmA, &raw_full[rs], x0 + b * raw_box_elems(C::FMT),
-                                        tm * C::BM);
+                            tma_load_2d_hint(dst + b * 16384, &tmA, &raw_full[rs], x0 + b * raw_box_elems(C::FMT),
+                                             tm * C::BM, wpol);
                     }
                     __syncwarp();
                 }
