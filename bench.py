@@ -294,51 +294,76 @@ def run_device(torch, tb, sw: Sweep, steps: int, warmup: int, dist: Dist):
 
 def run_e2e(torch, tb, sw: Sweep, steps: int, warmup: int):
     """The same GEMMs through the C ABI with host inputs and outputs: every
-    GEMM copies its operands from pinned host memory, runs, and copies D back."""
+    GEMM copies its operands from pinned host memory, runs, and copies D back.
+    Copies and kernels are pipelined over three streams with two buffer sets:
+    the host->device copies of GEMM j+1 and the device->host copy of GEMM j-1
+    overlap GEMM j (PCIe carries both directions at once); each stream waits
+    only on the events of the buffers it reuses."""
     M, N, K = sw.M, sw.N, sw.K
     hA = {n: sw.Aq[n].cpu().pin_memory() for n in FORMATS}
     hB16 = sw.B16.cpu().pin_memory()
     hN = {n: (v[1].cpu().pin_memory(), v[2].cpu().pin_memory()) for n, v in sw.native.items()}
-    hD = torch.empty(M, N, dtype=torch.float32).pin_memory()
-    dA = torch.empty(max(a.numel() for a in sw.Aq.values()), dtype=torch.uint8, device="cuda")
-    dB = torch.empty(sw.B16.numel(), dtype=torch.uint8, device="cuda")
-    dB8 = torch.empty(max(v[2].numel() for v in sw.native.values()), dtype=torch.uint8, device="cuda")
-    h2d = d2h = 0
+    hD = [torch.empty(M, N, dtype=torch.float32).pin_memory() for _ in range(2)]
+    amax = max(max(a.numel() for a in sw.Aq.values()), max(v[1].numel() for v in sw.native.values()))
+    bmax = max(sw.B16.numel() * sw.B16.element_size(), max(v[2].numel() for v in sw.native.values()))
+    dA = [torch.empty(amax, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    dB = [torch.empty(bmax, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    dD = [torch.empty(M, N, dtype=torch.float32, device="cuda") for _ in range(2)]
+    s_in, s_run, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    hB16b = hB16.view(torch.uint8).reshape(-1)
+
+    # (label, host A, host B (bytes), kernel launcher(dA, dB, dD, stream))
+    jobs = []
+    for name in FORMATS:
+        f, al = sw.fmt[name], sw.alpha[name]
+        jobs.append((hA[name], hB16b, lambda a, b, d, st, f=f, al=al: tb.gemm_fused(
+            f, a, b, d, M, N, K, out=tb.Out.F32, alpha=al, stream=st)))
+        jobs.append((hA[name], hB16b, lambda a, b, d, st, f=f, al=al: (
+            tb.decode(f, a, sw.A16, M * K, stream=st),
+            tb.gemm_f16(sw.A16, b, d, M, N, K, out=tb.Out.F32, alpha=al, stream=st))))
+    for name, (f, _, _, al) in sw.native.items():
+        ha, hb = hN[name]
+        jobs.append((ha, hb, lambda a, b, d, st, f=f, al=al: tb.gemm_native(
+            f, a, f, b, d, M, N, K, out=tb.Out.F32, alpha=al, stream=st)))
+    h2d = sum(a.numel() + b.numel() for a, b, _ in jobs)
+    d2h = len(jobs) * hD[0].numel() * 4
+    ev_in, ev_run, ev_out = [None, None], [None, None], [None, None]
 
     def step():
-        nonlocal h2d, d2h
-        h2d = d2h = 0
-        for name in FORMATS:
-            f, al = sw.fmt[name], sw.alpha[name]
-            n = hA[name].numel()
-            dA[:n].copy_(hA[name], non_blocking=True)
-            dB.copy_(hB16, non_blocking=True)
-            tb.gemm_fused(f, dA, dB, sw.Dunf, M, N, K, out=tb.Out.F32, alpha=al)
-            hD.copy_(sw.Dunf, non_blocking=True)
-            dA[:n].copy_(hA[name], non_blocking=True)
-            dB.copy_(hB16, non_blocking=True)
-            tb.decode(f, dA, sw.A16, M * K)
-            tb.gemm_f16(sw.A16, dB, sw.Dunf, M, N, K, out=tb.Out.F32, alpha=al)
-            hD.copy_(sw.Dunf, non_blocking=True)
-            h2d += 2 * (n + hB16.numel())
-            d2h += 2 * hD.numel() * 4
-        for name, (f, _, _, al) in sw.native.items():
-            ha, hb = hN[name]
-            dA[:ha.numel()].copy_(ha, non_blocking=True)
-            dB8[:hb.numel()].copy_(hb, non_blocking=True)
-            tb.gemm_native(f, dA, f, dB8, sw.Dnat[name], M, N, K, out=tb.Out.F32, alpha=al)
-            hD.copy_(sw.Dnat[name], non_blocking=True)
-            h2d += ha.numel() + hb.numel()
-            d2h += hD.numel() * 4
+        for j, (ha, hb, run) in enumerate(jobs):
+            k = j & 1
+            with torch.cuda.stream(s_in):
+                if ev_run[k] is not None:
+                    s_in.wait_event(ev_run[k])  # the kernels that read this input slot are done
+                dA[k][:ha.numel()].copy_(ha.view(torch.uint8).reshape(-1), non_blocking=True)
+                dB[k][:hb.numel()].copy_(hb.reshape(-1), non_blocking=True)
+                ev_in[k] = torch.cuda.Event()
+                ev_in[k].record(s_in)
+            s_run.wait_event(ev_in[k])
+            if ev_out[k] is not None:
+                s_run.wait_event(ev_out[k])  # this output slot has been copied out
+            run(dA[k], dB[k], dD[k], s_run)
+            ev_run[k] = torch.cuda.Event()
+            ev_run[k].record(s_run)
+            s_out.wait_event(ev_run[k])
+            with torch.cuda.stream(s_out):
+                hD[k].copy_(dD[k], non_blocking=True)
+                ev_out[k] = torch.cuda.Event()
+                ev_out[k].record(s_out)
 
+    cur = torch.cuda.current_stream()
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(cur)
+    for st in (s_in, s_run, s_out):
+        st.wait_event(e0)
     for _ in range(steps):
         step()
-    e1.record()
+    for st in (s_in, s_run, s_out):
+        cur.wait_stream(st)
+    e1.record(cur)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     return ms, h2d, d2h
