@@ -519,7 +519,8 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     }
 
     // Pairs of SMs for the operand-loading kinds when the tiles are wide and
-    // plentiful (one 256 x 256 tile per cluster, no split).
+    // plentiful (256 x 256 tiles per cluster, those of a partial last wave as
+    // 256 x 128 halves; no split).
     const bool loading = r.kind == GemmKind::kF16 || r.kind == GemmKind::kNative || r.kind == GemmKind::kInt8;
     if (loading && bn == 256 && splits == 1 && r.M >= 256 && !r.force_bn && !r.force_splits) {
         const int mode = r.kind == GemmKind::kF16 ? kModeF16 : r.kind == GemmKind::kNative ? kModeNative8 : kModeInt8;
