@@ -500,6 +500,7 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     a.tiles_m = tiles_m; a.tiles_n = tiles_n; a.splits = splits;
     a.kb_per_split = kb_per; a.num_kb = num_kb;
     a.num_units = tiles_m * tiles_n * splits;
+    a.half_from = a.num_units;  // no half tiles unless set below (one-CTA kernel)
     a.alpha = r.alpha;
     a.D = r.D; a.ldd = r.ldd;
     a.out_f16 = r.out_f16;
@@ -561,6 +562,18 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
                 case kTF32: return run_fused_pair<kTF32>(r, a, clusters, st, why);
                 default: break;
             }
+        }
+    }
+
+    // One-CTA kernel, 256-column tiles without a split: the R tiles of a
+    // partial last wave (or all tiles, when fewer than the SMs) run as 2R
+    // halves of 128 columns when those fit in one wave.
+    if (bn == 256 && splits == 1) {
+        const int tiles = a.num_units;
+        const int rem = tiles > sms ? tiles % sms : tiles;
+        if (rem > 0 && 2 * rem <= sms) {
+            a.half_from = tiles - rem;
+            a.num_units = tiles + rem;
         }
     }
 

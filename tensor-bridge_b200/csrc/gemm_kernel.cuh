@@ -145,6 +145,9 @@ struct GemmCfg {
     // OR'd in at run time from GemmArgs::idesc_ab), FP32 accumulation,
     // K-major operands.
     static constexpr uint32_t IDESC = MODE == kModeInt8 ? idesc_i8(BM, BN) : idesc_make(0u, 0u, BM, BN);
+    // MMAs of a half tile (N = BN / 2; the launcher splits only BN = 256 tiles).
+    static constexpr uint32_t IDESC_HALF =
+        BN < 32 ? IDESC : (MODE == kModeInt8 ? idesc_i8(BM, BN / 2) : idesc_make(0u, 0u, BM, BN / 2));
 
     // Decode work per k-block: 16-byte raw units per row and in total, and
     // units per decode thread.
@@ -181,6 +184,10 @@ struct GemmArgs {
     // 256 x 128 halves each.  tx_b_half: TMA bytes of 64 B rows.
     int pair_full;
     uint32_t tx_b_half;
+    // One-CTA kernel (k_gemm): units [half_from, num_units) are the two
+    // BN / 2-column halves of the tiles from half_from on (a partial last wave
+    // split along N; == num_units when there are none).
+    int half_from;
 };
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) ----------------------
@@ -287,6 +294,20 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& p, int u, int& tm, i
     const int r = u / p.tiles_m;
     tn = r % p.tiles_n;
     sp = r / p.tiles_n;
+}
+
+// unit_coords for k_gemm, whose units from p.half_from on are halves of tiles:
+// half = 0 for a whole tile, 1 or 2 for its first or second BN / 2 columns.
+// Splitting a partial last wave along N keeps every output element one
+// accumulation over its K range in the same order.
+__device__ __forceinline__ void unit_coords_h(const GemmArgs& p, int u, int& tm, int& tn, int& sp, int& half) {
+    half = 0;
+    if (u >= p.half_from) {
+        const int h = u - p.half_from;
+        u = p.half_from + (h >> 1);
+        half = 1 + (h & 1);
+    }
+    unit_coords(p, u, tm, tn, sp);
 }
 
 __device__ __forceinline__ void unit_kblocks(const GemmArgs& p, int sp, int& kb0, int& kb1) {
@@ -441,8 +462,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             const uint32_t kTx =
                 C::kNativeLike ? p.tx_bytes : C::B_BYTES + (C::kDecode ? 0u : static_cast<uint32_t>(C::A_BYTES));
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-                int tm, tn, sp, kb0, kb1;
-                unit_coords(p, u, tm, tn, sp);
+                int tm, tn, sp, kb0, kb1, half;
+                unit_coords_h(p, u, tm, tn, sp, half);
                 unit_kblocks(p, sp, kb0, kb1);
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!__all_sync(0xFFFFFFFFu, mbar_wait(&b_empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
@@ -451,7 +472,9 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                         if constexpr (!C::kDecode)
                             tma_load_2d(smem + C::OFF_A + s * C::A_BYTES, &tmA, &b_full[s], kb * C::KB_ELEMS,
                                         tm * C::BM);
-                        tma_load_2d(smem + C::OFF_B + s * C::B_BYTES, &tmB, &b_full[s], kb * C::B_X_STEP, tn * C::BN);
+                        // (A half tile's box still has BN rows; its MMAs read the first BN / 2.)
+                        tma_load_2d(smem + C::OFF_B + s * C::B_BYTES, &tmB, &b_full[s], kb * C::B_X_STEP,
+                                    tn * C::BN + (half == 2 ? C::BN / 2 : 0));
                     }
                     __syncwarp();
                     ++issued;
@@ -472,14 +495,15 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             int t = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x, ++t) {
-                int tm, tn, sp, kb0, kb1;
-                unit_coords(p, u, tm, tn, sp);
+                int tm, tn, sp, kb0, kb1, half;
+                unit_coords_h(p, u, tm, tn, sp, half);
                 unit_kblocks(p, sp, kb0, kb1);
                 const int acc = t & 1;
                 const uint32_t aph = (t >> 1) & 1;
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag))) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::NACC * C::BN);
+                const uint32_t idesc = half ? C::IDESC_HALF : C::IDESC;
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!__all_sync(0xFFFFFFFFu, mbar_wait(&b_full[bs], bph, abort_flag))) { ok = false; break; }
                     tc_fence_after();
@@ -492,10 +516,10 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                             const uint32_t d = d_tmem + static_cast<uint32_t>((kk % C::NACC) * C::BN);
                             const uint64_t ad = sdesc_make(a_lo + 2u * kk), bd = sdesc_make(b_lo + 2u * kk);
                             if constexpr (C::MODE == kModeNative8)
-                                mma_f8f6f4_ss(d, ad, bd, C::IDESC | p.idesc_ab, accum);
+                                mma_f8f6f4_ss(d, ad, bd, idesc | p.idesc_ab, accum);
                             else if constexpr (C::MODE == kModeInt8)
-                                mma_i8_ss(d, ad, bd, C::IDESC, accum);
-                            else mma_f16_ss(d, ad, bd, C::IDESC, accum);
+                                mma_i8_ss(d, ad, bd, idesc, accum);
+                            else mma_f16_ss(d, ad, bd, idesc, accum);
                         }
                         mma_commit(&b_empty[bs]);
                     }
@@ -525,8 +549,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
         int t = 0;
         for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++t) {
-            int tm, tn, sp;
-            unit_coords(p, u, tm, tn, sp);
+            int tm, tn, sp, half;
+            unit_coords_h(p, u, tm, tn, sp, half);
             const int acc = t & 1;
             const uint32_t aph = (t >> 1) & 1;
             const bool ok = mbar_wait(&acc_full[acc], aph, abort_flag);
@@ -535,8 +559,10 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             const int row = tm * C::BM + quarter * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                    static_cast<uint32_t>(acc * C::NACC * C::BN);
+            const int ncols = half ? C::BN / 2 : C::BN;
+            const int col0 = tn * C::BN + (half == 2 ? C::BN / 2 : 0);
 #pragma unroll 1
-            for (int c = 0; c < C::BN; c += C::CW) {
+            for (int c = 0; c < ncols; c += C::CW) {
                 uint32_t v[C::CW];
                 tmem_ld_chunk<C::CW>(t_row + c, v);
                 if constexpr (C::NACC > 1) {
@@ -551,7 +577,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                     }
                 }
                 tmem_wait_ld();
-                store_row_chunk<C::CW>(p, sp, row, tn * C::BN + c, v);
+                store_row_chunk<C::CW>(p, sp, row, col0 + c, v);
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
@@ -565,8 +591,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                 long long issued = 0;
                 bool ok = true;
                 for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-                    int tm, tn, sp, kb0, kb1;
-                    unit_coords(p, u, tm, tn, sp);
+                    int tm, tn, sp, kb0, kb1, half;
+                    unit_coords_h(p, u, tm, tn, sp, half);
                     unit_kblocks(p, sp, kb0, kb1);
                     for (int kb = kb0; kb < kb1; kb += C::RK) {
                         if (!__all_sync(0xFFFFFFFFu, mbar_wait(&a_empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
@@ -603,8 +629,8 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             uint32_t aph = 0, dph = 0;  // raw ring; operand ring (same order as the B producer)
             bool ok = true;
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
-                int tm, tn, sp, kb0, kb1;
-                unit_coords(p, u, tm, tn, sp);
+                int tm, tn, sp, kb0, kb1, half;
+                unit_coords_h(p, u, tm, tn, sp, half);
                 unit_kblocks(p, sp, kb0, kb1);
                 for (int kb = kb0; kb < kb1; kb += C::DK) {
                     const int cnt = min(C::DK, kb1 - kb);
