@@ -750,6 +750,15 @@ def profile_case(case: str):
     tb = load_package()
     fname, shape = case.split(":")
     M, N, K = (int(v) for v in shape.lower().split("x"))
+    if fname == "e4m3xe4m3":  # the native FP8 GEMM (both operands E4M3, per-tensor scales)
+        A, sa = weights_q(torch, tb, tb.Format.E4M3, M, K, 0.02, seed=1)
+        B, sb = weights_q(torch, tb, tb.Format.E4M3, N, K, 1.0, seed=2)
+        D = torch.empty(M, N, dtype=torch.float32, device="cuda")
+        for _ in range(5):
+            tb.gemm_native(tb.Format.E4M3, A, tb.Format.E4M3, B, D, M, N, K, alpha=sa * sb)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": case, "ok": True}))
+        return
     if fname == "f16":  # the plain FP16 GEMM
         A = torch.randn(M, K, device="cuda").half()
         B = torch.randn(N, K, device="cuda").half()
@@ -789,7 +798,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the MLP-shape and 8192^3 FP4 sub-objects")
     ap.add_argument("--profile-case", metavar="FMT:MxNxK",
                     help="run only 5 fused weight-only GEMMs of this case (e.g. e4m3:14336x16x4096; f16:MxNxK for "
-                         "the plain FP16 GEMM) and exit; "
+                         "the plain FP16 GEMM, e4m3xe4m3:MxNxK for the native FP8 GEMM) and exit; "
                          "the command profiles/ captures of single kernels use")
     args = ap.parse_args()
     if args.profile_case:
