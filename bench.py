@@ -528,6 +528,18 @@ def decode_streams(torch, tb, peaks, rows: int = 14336, cols: int = 4096, iters:
         out[name] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
                      "pct_hbm": 100 * nbytes / ms / 1e6 / peaks["hbm_gbs"]}
         del pairs, A
+    # Block-scaled FP4: packed codes + one E4M3 scale byte per 16 values.
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    q = torch.randint(0, 256, (n // 2,), generator=g, device="cuda", dtype=torch.uint8)
+    sc = torch.randint(0x20, 0x60, (n // 16,), generator=g, device="cuda", dtype=torch.uint8)
+    trip = [(q, sc, torch.empty(n, dtype=torch.float16, device="cuda")),
+            (q.clone(), sc.clone(), torch.empty(n, dtype=torch.float16, device="cuda"))]
+    ms = time_graph(torch, [lambda q=q, s=s, d=d: tb.decode_nvfp4(q, s, d, n) for q, s, d in trip] * 2, iters)
+    nbytes = n // 2 + n // 16 + 2 * n
+    out["nvfp4"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                    "pct_hbm": 100 * nbytes / ms / 1e6 / peaks["hbm_gbs"]}
+    del trip, q, sc
     return out
 
 

@@ -105,6 +105,19 @@ tb_status tb_decode(tb_format fmt, const void* src, uint16_t* dst, size_t n, tb_
 tb_status tb_decode_transposed(tb_format fmt, const void* src, uint16_t* dst,
                                int rows, int cols, tb_stream_t stream);
 
+/* Block-scaled FP4 (the NVFP4 layout that fp4.h:6 names; the reference has no
+ * kernel for it): dst[i] = e2m1(code i) * e4m3(scales[i / 16]) as FP16 bits,
+ * i < n, n a multiple of 16.  `src` holds the codes packed two per byte in
+ * the reference order (element 2j in the HIGH nibble of byte j, fp4.h:37-43;
+ * codes as fp4_e2m1_to_half, fp4.h:33-35); `scales` holds one byte per 16
+ * consecutive values, so a [rows x cols] matrix (cols a multiple of 16) has
+ * [rows x cols/16] row-major scales.  Scale bytes are OCP E4M3 with
+ * subnormals (exponent 0: m * 2^-9); 0x7F and 0xFF are NaN and give 0x7E00.
+ * Every product is an FP16 value, so the decode is exact; a per-tensor FP32
+ * scale goes into the GEMM's alpha (tb_gemm_f16). */
+tb_status tb_decode_nvfp4(const uint8_t* src, const uint8_t* scales, uint16_t* dst, size_t n,
+                          tb_stream_t stream);
+
 /* Reference-shaped decode entry points: A [M x K] decoded straight into
  * A16 [M x K], B [K x N] decoded transposed into B16 [N x K].  Either pair may
  * be NULL to skip that operand.  Mirror, in order:

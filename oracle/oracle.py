@@ -43,6 +43,9 @@ def lib():
         l.oracle_f32_to_f16.argtypes = [f]
         l.oracle_decode_e4m3_i8.argtypes = [p, p, sz, f]
         l.oracle_gemm_i8.argtypes = [p, p, p, i, i, i, i]
+        l.oracle_e4m3_scale_to_f32.restype = f
+        l.oracle_e4m3_scale_to_f32.argtypes = [ctypes.c_uint8]
+        l.oracle_decode_nvfp4.argtypes = [p, p, p, sz]
         _lib = l
     return _lib
 
@@ -126,6 +129,45 @@ def ref_cpu_gemm(a_fmt: int, A: np.ndarray, B16: np.ndarray, M: int, N: int, K: 
     r.ref_cpu_decode_gemm(a_fmt, _c(np.ascontiguousarray(A)), _c(np.ascontiguousarray(B16)), _c(out), M, N, K, r0, r1,
                           float(alpha), threads)
     return out
+
+
+def decode_nvfp4(q: np.ndarray, scales: np.ndarray, n: int) -> np.ndarray:
+    """Block-scaled FP4 -> FP16 bits: packed E2M1 codes (element 2j in the high
+    nibble of byte j) times one E4M3 scale byte per 16 values."""
+    q = np.ascontiguousarray(q, dtype=np.uint8).ravel()
+    scales = np.ascontiguousarray(scales, dtype=np.uint8).ravel()
+    if n % 16 or q.size < n // 2 or scales.size < n // 16:
+        raise ValueError(f"block-scaled FP4 of {n} values needs {n // 2} code bytes and {n // 16} scale bytes")
+    out = np.empty(n, dtype=np.uint16)
+    lib().oracle_decode_nvfp4(_c(q), _c(scales), _c(out), n)
+    return out
+
+
+def e4m3_scale_values() -> np.ndarray:
+    """All 256 scale bytes as float32 (OCP E4M3 with subnormals; 0x7F/0xFF NaN)."""
+    return np.array([lib().oracle_e4m3_scale_to_f32(c) for c in range(256)], dtype=np.float32)
+
+
+def quantize_nvfp4(x: np.ndarray):
+    """Two-level block-scaled FP4 of a [rows x cols] matrix (cols a multiple of
+    16): g = amax / (6 * 448); each 16-value block's scale is the E4M3 value
+    nearest to amax_block / (6 * g); codes = E2M1 of x / (scale * g) by the
+    reference's rounding (fp4.h:46-53).  Returns (packed codes, scale bytes, g)
+    with x ~= decode_nvfp4(codes, scales) * g."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    assert cols % 16 == 0
+    amax = float(np.max(np.abs(x))) if x.size else 0.0
+    g = np.float32(amax / (6.0 * 448.0)) if amax > 0 else np.float32(1.0)
+    blocks = x.reshape(rows, cols // 16, 16)
+    want = np.max(np.abs(blocks), axis=2) / (np.float32(6.0) * g)
+    table = e4m3_scale_values()[:127]  # positive finite codes, ascending
+    hi = np.clip(np.searchsorted(table, want), 1, 126)
+    code = np.where(np.abs(table[hi] - want) < np.abs(want - table[hi - 1]), hi, hi - 1).astype(np.uint8)
+    sv = table[code].astype(np.float32)[..., None] * g
+    y = np.where(sv > 0, blocks / np.where(sv > 0, sv, 1), 0).astype(np.float32)
+    q = quantize(E2M1, y.reshape(rows, cols), 1.0)
+    return q.reshape(rows, cols // 2), code.reshape(rows, cols // 16), float(g)
 
 
 def rel_frob(x: np.ndarray, ref: np.ndarray) -> float:

@@ -324,6 +324,36 @@ void oracle_decode_e4m3_i8(const uint8_t* src, int8_t* dst, size_t n, float scal
     for (size_t i = 0; i < n; i++) dst[i] = oracle_e4m3_to_i8(src[i], scale);
 }
 
+/* ---- block-scaled FP4 (the NVFP4 layout fp4.h:6 names; no reference kernel) -- */
+
+/* A scale byte read as OCP E4M3 with subnormals (exponent 0: m * 2^-9);
+ * 0x7F and 0xFF are NaN.  Unlike fp8_e4m3_to_half (fp8.h:23-31) nothing is
+ * flushed: block scales use the whole E4M3 range. */
+float oracle_e4m3_scale_to_f32(uint8_t s) {
+    const uint32_t e = (s >> 3) & 0x0Fu, m = s & 0x07u;
+    float v;
+    if (e == 15 && m == 7) return u2f(0x7FFFFFFFu);
+    if (e == 0) v = (float)m * 0.001953125f; /* m * 2^-9, exact */
+    else v = u2f(((e + 120u) << 23) | (m << 20));
+    return (s & 0x80u) ? -v : v;
+}
+
+/* Value i: the E2M1 code (packed two per byte, element 2j in the high nibble
+ * of byte j, fp4.h:37-43; values from the table of fp4.h:27-30) times the
+ * scale of its 16-value block, rounded to FP16 -- exact, every product being
+ * an FP16 value.  A NaN scale gives 0x7E00. */
+uint16_t oracle_nvfp4_at(const uint8_t* q, const uint8_t* scales, size_t i) {
+    const uint8_t s = scales[i / 16];
+    if ((s & 0x7Fu) == 0x7Fu) return 0x7E00u;
+    const uint8_t b = q[i / 2];
+    const uint16_t x = kE2M1[(i & 1) ? (b & 0x0Fu) : (b >> 4)];
+    return oracle_f32_to_f16(oracle_f16_to_f32(x) * oracle_e4m3_scale_to_f32(s));
+}
+
+void oracle_decode_nvfp4(const uint8_t* q, const uint8_t* scales, uint16_t* dst, size_t n) {
+    for (size_t i = 0; i < n; i++) dst[i] = oracle_nvfp4_at(q, scales, i);
+}
+
 /* gemm_int8_wmma, src/gemm.cu:58-70: D[M x N] = sum_k A8[m][k] * B8[n][k] with
  * 32-bit integer accumulation (B8 is the reference's column-major B, [N x K]
  * row-major).  Summed in 64 bits and wrapped to 32, as a 32-bit accumulator

@@ -49,6 +49,9 @@ void oracle_gemm(int a_fmt, const void* A, int b_fmt, const void* B, void* D, in
 int8_t oracle_e4m3_to_i8(uint8_t c, float scale);
 void oracle_decode_e4m3_i8(const uint8_t* src, int8_t* dst, size_t n, float scale);
 void oracle_gemm_i8(const int8_t* A, const int8_t* B, int32_t* D, int M, int N, int K, int nthreads);
+float oracle_e4m3_scale_to_f32(uint8_t s);
+uint16_t oracle_nvfp4_at(const uint8_t* q, const uint8_t* scales, size_t i);
+void oracle_decode_nvfp4(const uint8_t* q, const uint8_t* scales, uint16_t* dst, size_t n);
 
 #ifdef __cplusplus
 }

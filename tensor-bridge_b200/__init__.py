@@ -85,6 +85,7 @@ SIGNATURES = {
     "tb_device_error": (_st, [ctypes.POINTER(_i), _i]),
     "tb_decode": (_st, [_i, _p, _p, _sz, _p]),
     "tb_decode_transposed": (_st, [_i, _p, _p, _i, _i, _p]),
+    "tb_decode_nvfp4": (_st, [_p, _p, _p, _sz, _p]),
     "tb_decode_fp8_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "tb_decode_bf16_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "tb_decode_tf32_to_half": (_st, [_p, _p, _p, _p, _i, _i, _i, _p]),
@@ -174,6 +175,10 @@ def decode(fmt, src, dst, n: int, stream=None):
 
 def decode_transposed(fmt, src, dst, rows: int, cols: int, stream=None):
     call("tb_decode_transposed", int(fmt), _ptr(src), _ptr(dst), rows, cols, _stream(stream))
+
+
+def decode_nvfp4(src, scales, dst, n: int, stream=None):
+    call("tb_decode_nvfp4", _ptr(src), _ptr(scales), _ptr(dst), n, _stream(stream))
 
 
 def quantize(fmt, src, dst, n: int, scale: float = 1.0, stream=None):

@@ -131,6 +131,16 @@ tb_status tb_decode_transposed(tb_format fmt, const void* src, uint16_t* dst, in
     return from_cuda(tb::decode_transposed_launch(fmt, src, dst, rows, cols, stream), "transposed decode launch");
 }
 
+tb_status tb_decode_nvfp4(const uint8_t* src, const uint8_t* scales, uint16_t* dst, size_t n, tb_stream_t stream) {
+    if (n % 16) return fail(TB_ERR_SHAPE, "block-scaled FP4 needs a multiple of 16 values, got %zu", n);
+    if (n == 0) return TB_OK;
+    if (!src || !scales || !dst) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    const int sms = tb::device_info(tb::current_device()).sms;
+    return from_cuda(tb::decode_nvfp4_launch(src, scales, dst, n, stream, sms), "block-scaled FP4 decode launch");
+}
+
 static tb_status decode_pair(tb_format fmt, const void* A, const void* B, uint16_t* A16, uint16_t* B16, int M, int N,
                              int K, tb_stream_t stream) {
     if (M < 0 || N < 0 || K < 0) return fail(TB_ERR_SHAPE, "negative shape");

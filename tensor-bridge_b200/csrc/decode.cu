@@ -356,6 +356,89 @@ __global__ void __launch_bounds__(256) k_fp4_repack(const uint8_t* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------------
+// Block-scaled FP4 (NVFP4 layout): packed E2M1 codes in the reference order
+// (fp4.h:37-43, element 2j in the high nibble of byte j) and one E4M3 scale
+// byte per 16 consecutive values.  value = e2m1(code) * e4m3(scale).  Scale
+// bytes are read as OCP E4M3 with subnormals (exponent 0: m * 2^-9); 0x7F and
+// 0xFF are NaN and give 0x7E00.  Every product is an FP16 value (|v| in
+// [2^-10, 2688], at most six significant bits), so the FP16 multiply rounds
+// nothing and -0 follows the IEEE sign rule.
+
+// A scale byte as FP16 bits, duplicated into both halves.
+__device__ __forceinline__ uint32_t nvfp4_scale_x2(uint32_t s) {
+    const uint32_t e = (s >> 3) & 0xFu, m = s & 7u;
+    uint32_t h = e ? (((e + 8u) << 10) | (m << 7))
+                   : static_cast<uint32_t>(__half_as_ushort(__float2half_rn(static_cast<float>(m) * 0x1p-9f)));
+    h |= (s & 0x80u) << 8;
+    return h | (h << 16);
+}
+
+__device__ __forceinline__ uint32_t mul_f16x2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ bool nvfp4_scale_is_nan(uint32_t s) { return (s & 0x7Fu) == 0x7Fu; }
+
+// One item = 8 values: 4 packed bytes -> 16 bytes of FP16; items 2b and 2b+1
+// share scale byte b.  Same streaming scheme as k_decode_stream (16 items in
+// flight per thread, each warp instruction covering contiguous bytes).
+__global__ void __launch_bounds__(256) k_decode_nvfp4(const uint32_t* __restrict__ src,
+                                                      const uint8_t* __restrict__ scales, uint4* __restrict__ dst,
+                                                      size_t items) {
+    constexpr int kRep = 16;
+    constexpr size_t kChunk = 32 * kRep;
+    const int lane = threadIdx.x & 31;
+    const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const size_t nwarps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+    for (size_t base = warp * kChunk; base < items; base += nwarps * kChunk) {
+        uint32_t in[kRep], sc[kRep];
+#pragma unroll
+        for (int j = 0; j < kRep; ++j) {
+            const size_t it = base + j * 32 + lane;
+            if (it < items) {
+                in[j] = __ldcs(src + it);
+                sc[j] = __ldcs(scales + (it >> 1));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kRep; ++j) {
+            const size_t it = base + j * 32 + lane;
+            if (it < items) {
+                uint32_t o[4];
+                if (nvfp4_scale_is_nan(sc[j])) {
+                    o[0] = o[1] = o[2] = o[3] = 0x7E007E00u;
+                } else {
+                    decode_e2m1_packed_x8(in[j], o);
+                    const uint32_t s2 = nvfp4_scale_x2(sc[j]);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) o[k] = mul_f16x2(o[k], s2);
+                }
+                __stcs(dst + it, make_uint4(o[0], o[1], o[2], o[3]));
+            }
+        }
+    }
+}
+
+// Any alignment: one value per thread, grid-stride.
+__global__ void __launch_bounds__(256) k_decode_nvfp4_scalar(const uint8_t* __restrict__ src,
+                                                             const uint8_t* __restrict__ scales,
+                                                             uint16_t* __restrict__ dst, size_t n) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint32_t s = scales[i >> 4];
+        if (nvfp4_scale_is_nan(s)) {
+            dst[i] = 0x7E00u;
+            continue;
+        }
+        const uint8_t b = src[i >> 1];
+        const uint32_t x = tensor_bridge::e2m1_to_half_bits((i & 1) ? (b & 0xFu) : (b >> 4));
+        dst[i] = static_cast<uint16_t>(mul_f16x2(x, nvfp4_scale_x2(s)) & 0xFFFFu);
+    }
+}
+
+// ---------------------------------------------------------------------------------
 // Host launchers
 
 static size_t in_bytes_of(int fmt, size_t n) {
@@ -450,6 +533,23 @@ cudaError_t decode_e4m3_i8_transposed_launch(const uint8_t* src, int8_t* dst, in
 cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms) {
     const size_t blocks = std::max<size_t>(1, std::min<size_t>((n / 16 + 255) / 256, static_cast<size_t>(sms) * 8));
     k_fp4_repack<<<static_cast<unsigned>(blocks), 256, 0, st>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
+cudaError_t decode_nvfp4_launch(const uint8_t* src, const uint8_t* scales, uint16_t* dst, size_t n,
+                                cudaStream_t st, int sms) {
+    const bool aligned = (reinterpret_cast<uintptr_t>(src) & 3u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+    if (!aligned) {
+        const size_t blocks = std::min<size_t>((n + 255) / 256, static_cast<size_t>(sms) * 8);
+        k_decode_nvfp4_scalar<<<static_cast<unsigned>(std::max<size_t>(blocks, 1)), 256, 0, st>>>(src, scales, dst,
+                                                                                                    n);
+        return cudaGetLastError();
+    }
+    const size_t items = n / 8;  // n is a multiple of 16
+    const size_t blocks = std::max<size_t>(1, std::min<size_t>((items + 8 * 32 * 16 - 1) / (8 * 32 * 16),
+                                                               static_cast<size_t>(sms) * 8));
+    k_decode_nvfp4<<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const uint32_t*>(src), scales,
+                                                                  reinterpret_cast<uint4*>(dst), items);
     return cudaGetLastError();
 }
 
