@@ -761,6 +761,19 @@ def profile_case(case: str):
     import torch
     tb = load_package()
     fname, shape = case.split(":")
+    if fname == "nvfp4":  # the block-scaled FP4 decode streamer on a ROWS x COLS weight
+        rows, cols = (int(v) for v in shape.lower().split("x"))
+        n = rows * cols
+        g = torch.Generator(device="cuda")
+        g.manual_seed(11)
+        q = torch.randint(0, 256, (n // 2,), generator=g, device="cuda", dtype=torch.uint8)
+        sc = torch.randint(0x20, 0x60, (n // 16,), generator=g, device="cuda", dtype=torch.uint8)
+        d = torch.empty(n, dtype=torch.float16, device="cuda")
+        for _ in range(5):
+            tb.decode_nvfp4(q, sc, d, n)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": case, "ok": True}))
+        return
     M, N, K = (int(v) for v in shape.lower().split("x"))
     if fname == "e4m3xe4m3":  # the native FP8 GEMM (both operands E4M3, per-tensor scales)
         A, sa = weights_q(torch, tb, tb.Format.E4M3, M, K, 0.02, seed=1)
@@ -810,7 +823,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the MLP-shape and 8192^3 FP4 sub-objects")
     ap.add_argument("--profile-case", metavar="FMT:MxNxK",
                     help="run only 5 fused weight-only GEMMs of this case (e.g. e4m3:14336x16x4096; f16:MxNxK for "
-                         "the plain FP16 GEMM, e4m3xe4m3:MxNxK for the native FP8 GEMM) and exit; "
+                         "the plain FP16 GEMM, e4m3xe4m3:MxNxK for the native FP8 GEMM, nvfp4:ROWSxCOLS for 5 "
+                         "block-scaled FP4 decodes) and exit; "
                          "the command profiles/ captures of single kernels use")
     args = ap.parse_args()
     if args.profile_case:
