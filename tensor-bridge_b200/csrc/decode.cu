@@ -383,7 +383,10 @@ __device__ __forceinline__ bool nvfp4_scale_is_nan(uint32_t s) { return (s & 0x7
 
 // One item = 8 values: 4 packed bytes -> 16 bytes of FP16; items 2b and 2b+1
 // share scale byte b.  Same streaming scheme as k_decode_stream (16 items in
-// flight per thread, each warp instruction covering contiguous bytes).
+// flight per thread, each warp instruction covering contiguous bytes).  The
+// 256 scale bytes of a warp's 512-item chunk come in as one 8-byte load per
+// lane (lane l holds chunk bytes 8l..8l+7); item j of lane l needs chunk byte
+// 16j + l/2, which lane 2j + l/16 holds at offset (l/2) % 8.
 __global__ void __launch_bounds__(256) k_decode_nvfp4(const uint32_t* __restrict__ src,
                                                       const uint8_t* __restrict__ scales, uint4* __restrict__ dst,
                                                       size_t items) {
@@ -392,15 +395,36 @@ __global__ void __launch_bounds__(256) k_decode_nvfp4(const uint32_t* __restrict
     const int lane = threadIdx.x & 31;
     const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const size_t nwarps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+    const size_t nsc = items >> 1;
     for (size_t base = warp * kChunk; base < items; base += nwarps * kChunk) {
         uint32_t in[kRep], sc[kRep];
+        const size_t s0 = (base >> 1) + 8 * lane;
+        uint32_t wx = 0, wy = 0;
+        if (s0 + 8 <= nsc) {
+            const uint2 w = __ldcs(reinterpret_cast<const uint2*>(scales + s0));
+            wx = w.x;
+            wy = w.y;
+        } else {
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+                if (s0 + b < nsc) {
+                    const uint32_t v = __ldcs(scales + s0 + b);
+                    if (b < 4) wx |= v << (8 * b);
+                    else wy |= v << (8 * (b - 4));
+                }
+        }
 #pragma unroll
         for (int j = 0; j < kRep; ++j) {
             const size_t it = base + j * 32 + lane;
-            if (it < items) {
-                in[j] = __ldcs(src + it);
-                sc[j] = __ldcs(scales + (it >> 1));
-            }
+            if (it < items) in[j] = __ldcs(src + it);
+        }
+        const int byte = (lane >> 1) & 7;
+#pragma unroll
+        for (int j = 0; j < kRep; ++j) {
+            const int from = 2 * j + (lane >> 4);
+            const uint32_t x = __shfl_sync(0xFFFFFFFFu, wx, from);
+            const uint32_t y = __shfl_sync(0xFFFFFFFFu, wy, from);
+            sc[j] = ((byte < 4 ? x : y) >> (8 * (byte & 3))) & 0xFFu;
         }
 #pragma unroll
         for (int j = 0; j < kRep; ++j) {
@@ -538,7 +562,8 @@ cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaSt
 
 cudaError_t decode_nvfp4_launch(const uint8_t* src, const uint8_t* scales, uint16_t* dst, size_t n,
                                 cudaStream_t st, int sms) {
-    const bool aligned = (reinterpret_cast<uintptr_t>(src) & 3u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+    const bool aligned = (reinterpret_cast<uintptr_t>(src) & 3u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0 &&
+                         (reinterpret_cast<uintptr_t>(scales) & 7u) == 0;
     if (!aligned) {
         const size_t blocks = std::min<size_t>((n + 255) / 256, static_cast<size_t>(sms) * 8);
         k_decode_nvfp4_scalar<<<static_cast<unsigned>(std::max<size_t>(blocks, 1)), 256, 0, st>>>(src, scales, dst,
