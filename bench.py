@@ -566,26 +566,55 @@ def int8_square(torch, tb, n: int = 4096, iters: int = 10):
             "fp8_fused_int8_tops": ops / ms_f / 1e9}
 
 
-def fp4_square(torch, tb, peaks, n: int = 8192, iters: int = 40):
-    """Large square fused GEMM: A packed E2M1 from N(0, 1) with scale 6/maxabs,
-    B FP16 N(0, 1), FP32 accumulation, FP16 output.  The SM clocks and power
-    are sampled every 10 ms over this section alone ("clocks"): a GEMM at this
-    rate runs into the 1 kW power cap, which lowers the clock."""
+def fused_square(torch, tb, peaks, fmt_name: str = "e2m1", n: int = 8192, iters: int = 40):
+    """Large square fused GEMM: A packed E2M1 (or E4M3) from N(0, 1) with scale
+    FORMAT_MAX/maxabs, B FP16 N(0, 1), FP32 accumulation, FP16 output.  The SM
+    clocks and power are sampled every 10 ms over this section alone
+    ("clocks"): a GEMM at this rate runs into the 1 kW power cap, which lowers
+    the clock."""
+    fmt = tb.Format.E2M1 if fmt_name == "e2m1" else tb.Format.E4M3
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
-    A, alpha = weights_q(torch, tb, tb.Format.E2M1, n, n, 1.0, seed=8192)
+    A, alpha = weights_q(torch, tb, fmt, n, n, 1.0, seed=8192)
     g = torch.Generator(device="cuda")
     g.manual_seed(8193)
     B = torch.randn(n, n, generator=g, device="cuda").half()
     D = torch.empty(n, n, dtype=torch.float16, device="cuda")
     clocks = ClockSampler(torch.cuda.current_device(), interval_ms=10)
     clocks.start()
-    ms = time_each(torch, lambda: tb.gemm_fused(tb.Format.E2M1, A, B, D, n, n, n, out=tb.Out.F16, alpha=alpha),
-                   iters, flush)
+    ms = time_each(torch, lambda: tb.gemm_fused(fmt, A, B, D, n, n, n, out=tb.Out.F16, alpha=alpha), iters, flush)
     clk = clocks.stop()
     tf = 2.0 * n ** 3 / ms / 1e9
-    return {"M": n, "N": n, "K": n, "fmt": "e2m1 packed", "out": "f16", "ms": ms, "tflops": tf,
-            "pct_f16_dense_peak_nominal": 100 * tf / 2250.0,
+    return {"M": n, "N": n, "K": n, "fmt": "e2m1 packed" if fmt_name == "e2m1" else "e4m3", "out": "f16",
+            "ms": ms, "tflops": tf, "pct_f16_dense_peak_nominal": 100 * tf / 2250.0,
             "frac_of_measured_bf16": tf / peaks["bf16_tflops"], "clocks": clk}
+
+
+def config_256(torch, tb, iters: int = 50):
+    """The 256 x 256 x 256 FP8 E4M3 weight-only GEMM: A from U[-1, 1] (seed 0)
+    quantized with scale 448/maxabs, B from U[-1, 1] (seed 1) in FP16; fused
+    decode + GEMM, FP32 out.  Reports its device time (median, one launch per
+    event pair) and its relative Frobenius error against the unquantized FP32
+    product, the measure the reference publishes for this case."""
+    n = 256
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    a = torch.rand(n, n, generator=g, device="cuda") * 2 - 1
+    g.manual_seed(1)
+    b = torch.rand(n, n, generator=g, device="cuda") * 2 - 1
+    amax = torch.zeros(1, dtype=torch.float32, device="cuda")
+    tb.absmax(a, a.numel(), amax)
+    scale = float(np.float32(448.0) / np.float32(float(amax.item())))
+    A = torch.empty(n * n, dtype=torch.uint8, device="cuda")
+    tb.quantize(tb.Format.E4M3, a, A, n * n, scale=scale)
+    B = b.half()
+    D = torch.empty(n, n, dtype=torch.float32, device="cuda")
+    alpha = float(np.float32(1.0) / np.float32(scale))
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    ms = time_each(torch, lambda: tb.gemm_fused(tb.Format.E4M3, A, B, D, n, n, n, alpha=alpha), iters, flush)
+    want = a.double() @ b.double().T
+    err = float(torch.linalg.norm(D.double() - want) / torch.linalg.norm(want))
+    return {"M": n, "N": n, "K": n, "fmt": "e4m3", "us": ms * 1e3, "tflops": 2.0 * n ** 3 / ms / 1e9,
+            "rel_frob_vs_unquantized_fp32": err}
 
 
 def sharded_weight_gemm(torch, tb, dist, steps: int = 5, warmup: int = 2):
@@ -607,6 +636,14 @@ def sharded_weight_gemm(torch, tb, dist, steps: int = 5, warmup: int = 2):
     rows = W if world == 1 else tb.shard_rows(W, M, world, chunks, rank)
     A = torch.empty(rows.numel(), dtype=torch.uint8, device="cuda")
     tb.quantize(tb.Format.E4M3, rows, A, rows.numel(), scale=scale)
+    # Rows kept for the check after timing: 8 from each of the world*chunks
+    # row blocks (a block straddles 128-row tile boundaries at offsets that
+    # differ per block), computed by every rank or gathered from the others.
+    nblk = max(world * chunks, 8)
+    mc = M // nblk
+    sample = torch.tensor(sorted({b * mc + (37 * b + 120 + 3 * i) % mc for b in range(nblk) for i in range(8)}),
+                          device="cuda")
+    W_s = W[sample].contiguous()
     del W, rows
     g.manual_seed(6)
     X = torch.randn(N, K, generator=g, device="cuda").half()
@@ -642,11 +679,38 @@ def sharded_weight_gemm(torch, tb, dist, steps: int = 5, warmup: int = 2):
     dist.barrier()
     if comm is not None:
         tb.nccl_comm_destroy(comm)
+    check = sharded_check(torch, tb, dist, W_s, sample, X, D, N, K, scale, alpha)
     flops = 2.0 * M * N * K
     return {"M": M, "N": N, "K": K, "fmt": "e4m3", "out": "f16", "world": world, "chunks": chunks,
             "scaling": "strong", "ms": ms, "tflops_total": flops / ms / 1e9,
             "tflops_per_gpu": flops / ms / 1e9 / world,
-            "allgather_bytes_per_rank": (world - 1) * (M // world) * N * 2 if world > 1 else 0}
+            "allgather_bytes_per_rank": (world - 1) * (M // world) * N * 2 if world > 1 else 0,
+            "check": check}
+
+
+def sharded_check(torch, tb, dist, W_s, sample, X, D, N: int, K: int, scale: float, alpha: float):
+    """Correctness of the sharded GEMM's D on every rank, on the sampled rows
+    of every row block (own and all-gathered): (1) bit for bit against the
+    single-GPU fused GEMM of the same quantized rows, run unsplit (same
+    kernel arithmetic, same K order), and (2) relative Frobenius error against
+    an FP64 product of the decoded rows (decode bit-exact to the reference's
+    primitives) and the FP16 activations.  Worst case over ranks."""
+    S = sample.numel()
+    A_s = torch.empty(S * K, dtype=torch.uint8, device="cuda")
+    tb.quantize(tb.Format.E4M3, W_s, A_s, S * K, scale=scale)
+    D_s = torch.empty(S, N, dtype=torch.float16, device="cuda")
+    tb.gemm_fused(tb.Format.E4M3, A_s, X, D_s, S, N, K, out=tb.Out.F16, alpha=alpha)  # no workspace: unsplit
+    A16 = torch.empty(S, K, dtype=torch.float16, device="cuda")
+    tb.decode(tb.Format.E4M3, A_s, A16, S * K)
+    torch.cuda.synchronize()
+    got = D[sample]
+    bitwise = bool(torch.equal(got.view(torch.int16), D_s.view(torch.int16)))
+    want = (A16.double() @ X.double().T) * alpha
+    err = float(torch.linalg.norm(got.double() - want) / torch.linalg.norm(want))
+    bad = dist.max(0.0 if bitwise else 1.0)
+    err = dist.max(err)
+    return {"rows_per_rank": S, "blocks": S // 8, "bitwise_vs_1gpu": bad == 0.0, "rel_frob_max_vs_fp64": err,
+            "pass": bad == 0.0 and err <= 1e-3}
 
 
 # ---- CPU baseline: the reference's own host path ---------------------------------------
@@ -685,10 +749,42 @@ def cpu_baseline(sw_shape, seconds: float = 12.0):
         run(f, A, al, (0, rows))
     dt = time.perf_counter() - t0
     flops = 2.0 * rows * N * K * len(data)
-    return {"value": flops / dt / 1e12, "unit": UNIT, "cores": threads,
-            "kind": "reference" if use_ref else "port",
-            "sample": f"{rows} rows x N={N} x K={K} of each of {len(data)} weight-only GEMMs "
-                      f"({', '.join(data)}), decode + FP32 loop, {dt:.1f} s"}
+    out = {"value": flops / dt / 1e12, "unit": UNIT, "cores": threads,
+           "kind": "reference" if use_ref else "port",
+           "sample": f"{rows} rows x N={N} x K={K} of each of {len(data)} weight-only GEMMs "
+                     f"({', '.join(data)}), decode + FP32 loop, {dt:.1f} s"}
+    if use_ref:
+        out["naive_single_thread"] = naive_loop_times(O)
+    return out
+
+
+def naive_loop_times(O):
+    """The reference's own naive single-thread CPU product (bench/bench_formats.cu:183-186:
+    decode, then for every (i, j) an FP32 sum over k with B read [K x N]) on
+    the 256^3 and 512^3 E4M3 weight-only cases, one host thread."""
+    res = {}
+    for n in (256, 512):
+        a, b = O.uniform(0, (n, n)), O.uniform(1, (n, n))
+        s = O.per_tensor_scale(a, O.E4M3)
+        A = O.quantize(O.E4M3, a, s)
+        B16 = O.f32_to_f16_bits(b).reshape(n, n)
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            O.ref_naive_gemm(O.E4M3, A, B16, n, n, n, alpha=float(np.float32(1) / np.float32(s)))
+            reps += 1
+            if time.perf_counter() - t0 > 1.0:
+                break
+        ms = (time.perf_counter() - t0) / reps * 1e3
+        res[f"{n}^3"] = {"ms": ms, "gflops": 2.0 * n ** 3 / ms / 1e6, "cores": 1}
+    return res
+
+
+def sweep_config(M: int, N: int, K: int, world: int) -> dict:
+    """The workload's `config` object, shared by both arms of the benchmark."""
+    return {"workload": f"format sweep {M}x{N}x{K}: fused + unfused decode+GEMM for TF32/BF16/E4M3/E2M1, "
+                        f"native E4M3xE4M3 and E2M1xE2M1; FP32 out", "M": M, "N": N, "K": K,
+            "gemms_per_step": 10, "l2": "flushed between steps (256 MiB write)",
+            "parallelism": f"replicas x{world}"}
 
 
 def reference_arm(args):
@@ -705,7 +801,9 @@ def reference_arm(args):
     b = O.normal(1, (N, K), 1.0)
     B16 = O.f32_to_f16_bits(b).reshape(N, K)
     fmts = {"tf32": O.TF32, "bf16": O.BF16, "e4m3": O.E4M3, "e2m1": O.E2M1}
-    rows = max(threads, 2 * threads)
+    # 8 rows per thread: B is widened once per GEMM call (in parallel), so the
+    # row loop dominates as it does in cpu_baseline's calibrated sample.
+    rows = 8 * threads
     data = []
     for name, f in fmts.items():
         a = O.normal(2, (rows, K), 0.02)
@@ -734,8 +832,7 @@ def reference_arm(args):
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (decoded f16 operands)", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"format sweep {M}x{N}x{K} (bounded row sample on the host)", "M": M, "N": N,
-                       "K": K},
+            "config": sweep_config(M, N, K, 1),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads,
                              "kind": "reference" if use_ref else "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -846,7 +943,6 @@ def main():
     e2e_max = dist.max(e2e_ms)
     e2e_steps = max(2, args.steps // 2)
     q = quality(torch, tb, sw)
-    assert tb.device_error() == 0, "a kernel reported a device-side wait timeout"
 
     step_flops = sw.step_flops()
     value = dist.world * step_flops * args.steps / (t_max / 1e3) / 1e12
@@ -896,10 +992,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16xf16->f32 (decoded operands); e4m3xe4m3, e2m1xe2m1->f32 native",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": f"format sweep {M}x{N}x{K}: fused + unfused decode+GEMM for TF32/BF16/E4M3/E2M1, "
-                               f"native E4M3xE4M3 and E2M1xE2M1; FP32 out", "M": M, "N": N, "K": K,
-                   "gemms_per_step": len(sw.ops()) - len(FORMATS), "l2": "flushed between steps (256 MiB write)",
-                   "parallelism": f"replicas x{dist.world}"},
+        "config": sweep_config(M, N, K, dist.world),
         "roofline": roof,
         "e2e": {"value": dist.world * step_flops * e2e_steps / (e2e_max / 1e3) / 1e12, "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -914,9 +1007,13 @@ def main():
         # GEMM runs first: right after the seconds-long MLP section the GPU
         # sits under its power cap (measured 1612 MHz, 770 us a launch,
         # against 1965 MHz and 643 us three seconds later); its own clocks
-        # are recorded with it.
+        # are recorded with it, and it runs once more at the end ("after load").
         torch.cuda.empty_cache()
-        line["fp4_8192_fused"] = fp4_square(torch, tb, peaks)
+        line["fp4_8192_fused"] = fused_square(torch, tb, peaks, "e2m1")
+        torch.cuda.empty_cache()
+        line["e4m3_8192_fused"] = fused_square(torch, tb, peaks, "e4m3")
+        torch.cuda.empty_cache()
+        line["config_256_e4m3"] = config_256(torch, tb)
         torch.cuda.empty_cache()
         line["decode_stream_14336x4096"] = decode_streams(torch, tb, peaks)
         torch.cuda.empty_cache()
@@ -924,14 +1021,50 @@ def main():
         torch.cuda.empty_cache()
         line["int8_4096"] = int8_square(torch, tb)
         torch.cuda.empty_cache()
+        line["fp4_8192_fused_after_load"] = fused_square(torch, tb, peaks, "e2m1")
+        torch.cuda.empty_cache()
         # clocks over the extra sections (the headline's own are in "clocks")
         line["clocks_extras"] = extra_clocks.stop()
         line["sharded_weight_gemm"] = sharded_weight_gemm(torch, tb, dist)
+    assert tb.device_error() == 0, "a kernel reported a device-side wait timeout"
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline((M, N, K))
+    if not args.no_extra:
+        line["targets"] = targets(line)
     dist.close()
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def targets(line: dict) -> dict:
+    """The target figures in one compact object, printed last on the line."""
+    r = lambda v, d=1: None if v is None else round(float(v), d)
+    t = {}
+    f4, f4l, e4 = line["fp4_8192_fused"], line["fp4_8192_fused_after_load"], line["e4m3_8192_fused"]
+    t["fused_8192_pct_f16_dense_nominal"] = {"e2m1_rested": r(f4["pct_f16_dense_peak_nominal"]),
+                                             "e2m1_after_load": r(f4l["pct_f16_dense_peak_nominal"]),
+                                             "e4m3": r(e4["pct_f16_dense_peak_nominal"]), "goal": 70}
+    skinny = {}
+    for row in line["weight_only_mlp"]:
+        if row["tokens"] <= 16:
+            key = f"{row['W']}_{row['fmt']}"
+            lo, hi = skinny.get(key, (1e9, 0.0))
+            skinny[key] = (min(lo, row["fused_pct_hbm"]), max(hi, row["fused_pct_hbm"]))
+    t["skinny_pct_hbm_min_max"] = {k: [r(lo), r(hi)] for k, (lo, hi) in skinny.items()}
+    t["skinny_goal_pct_hbm"] = 80
+    fm = line["formats"]
+    t["fused_ge_unfused_4096"] = {k: fm[k]["fused_tflops"] >= fm[k]["unfused_tflops"] for k in FORMATS}
+    t["native_pct_fp8_dense"] = {k: r(fm[f"native_{k}"]["pct_fp8_dense_peak"]) for k in ("e4m3", "e2m1")}
+    t["int8_pct_i8_dense"] = r(line["int8_4096"]["pct_i8_dense_peak"])
+    sh = line["sharded_weight_gemm"]
+    t["sharded"] = {"world": sh["world"], "ms": r(sh["ms"], 3), "check_pass": sh["check"]["pass"],
+                    "rel_frob": float(f"{sh['check']['rel_frob_max_vs_fp64']:.2e}")}
+    c1 = line["config_256_e4m3"]
+    t["config_256"] = {"us": r(c1["us"], 2), "rel_frob_vs_fp32_pct": r(100 * c1["rel_frob_vs_unquantized_fp32"], 3)}
+    nv = (line.get("cpu_baseline") or {}).get("naive_single_thread")
+    if nv:
+        t["ref_naive_1thread_ms"] = {k: r(v["ms"], 2) for k, v in nv.items()}
+    return t
 
 
 if __name__ == "__main__":

@@ -34,9 +34,11 @@ constexpr uint16_t kFp4E2M1HalfBits[16] = {
 };
 
 #if defined(__CUDACC__)
-// Reference-named device table (fp4.h:27-30).  Kept for source compatibility;
-// the conversion functions below do not read it.
-static __device__ __constant__ unsigned short kFp4E2M1LUT[16] = {
+// Reference-named device table (fp4.h:27-30), declared as the reference
+// declares it (external linkage, so a translation unit that extern-declares
+// the table links against it).  Kept for source compatibility; the
+// conversion functions below do not read it.
+__device__ __constant__ unsigned short kFp4E2M1LUT[16] = {
     0x0000, 0x3800, 0x3C00, 0x3E00, 0x4000, 0x4200, 0x4400, 0x4600,
     0x8000, 0xB800, 0xBC00, 0xBE00, 0xC000, 0xC200, 0xC400, 0xC600,
 };

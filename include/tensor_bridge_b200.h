@@ -175,8 +175,13 @@ tb_status tb_gemm_f16(const uint16_t* A, const uint16_t* B, void* D, int M, int 
  * while the previous kernel on `stream` runs, if that kernel allows it (the
  * same kernel and its split-K reduction do), and then reads one-byte and FP4
  * weights before that kernel has finished; B, D, the workspace and BF16/TF32
- * weights are accessed only after it has.  Do not have a kernel that
- * triggers its dependents early write the weights of a following call. */
+ * weights are accessed only after it has.  CUDA makes the previous
+ * kernel's writes visible to this one only after the dependency wait, even
+ * when that kernel never triggers early (tb_quantize included): so the
+ * kernel launched just before this call on `stream` must not write its
+ * one-byte or FP4 weights.  Put an event, a stream synchronisation, a copy
+ * or any kernel launched without programmatic dependent launch between a
+ * writer of the weights and the GEMM. */
 tb_status tb_gemm_fused(tb_format a_fmt, const void* A, const uint16_t* B, void* D,
                         int M, int N, int K, tb_out_type out, float alpha,
                         void* workspace, size_t workspace_bytes, tb_stream_t stream);
@@ -192,8 +197,15 @@ size_t tb_gemm_fused_workspace(tb_format a_fmt, int M, int N, int K);
  * more than 20 MiB (tb_gemm_fused_workspace > 20 MiB; none on a 148-SM B200)
  * return TB_ERR_WORKSPACE.  The first call on each device does a one-time
  * set-up (looks up the array's device address) and should come before any
- * stream capture.  All calls on a device share the array, which keeps the last
- * call's contents; calls that overlap in time on different streams race on it. */
+ * stream capture.  The 20 MiB are device memory that the CUDA driver commits
+ * when it loads this part of the library on a device: at context creation
+ * under CUDA_MODULE_LOADING=EAGER, otherwise (lazy loading, the default since
+ * CUDA 12.2) during that first call, which then returns TB_ERR_CUDA if the
+ * host has already reserved all free device memory.  A host that reserves its
+ * memory pool up front should make one call (or run with eager loading)
+ * before it reserves the pool.  All calls on a device share the array, which
+ * keeps the last call's contents; calls that overlap in time on different
+ * streams race on it. */
 tb_status tb_gemm_fused_noalloc(tb_format a_fmt, const void* A, const uint16_t* B, void* D,
                                 int M, int N, int K, tb_out_type out, float alpha,
                                 tb_stream_t stream);

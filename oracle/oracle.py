@@ -61,6 +61,7 @@ def ref_lib():
                      "ref_fp32_to_bf16", "ref_half_to_bf16", "ref_fp32_to_tf32", "ref_fp32_to_half"):
             getattr(l, name).argtypes = [p, p, sz]
         l.ref_cpu_decode_gemm.argtypes = [i, p, p, p, i, i, i, i, i, f, i]
+        l.ref_naive_decode_gemm.argtypes = [i, p, p, p, i, i, i, f]
         _ref = l
     return _ref
 
@@ -128,6 +129,19 @@ def ref_cpu_gemm(a_fmt: int, A: np.ndarray, B16: np.ndarray, M: int, N: int, K: 
     out = np.empty((r1 - r0, N), dtype=np.float32)
     r.ref_cpu_decode_gemm(a_fmt, _c(np.ascontiguousarray(A)), _c(np.ascontiguousarray(B16)), _c(out), M, N, K, r0, r1,
                           float(alpha), threads)
+    return out
+
+
+def ref_naive_gemm(a_fmt: int, A: np.ndarray, B16_kn: np.ndarray, M: int, N: int, K: int,
+                   alpha: float = 1.0) -> np.ndarray:
+    """The reference's naive single-thread check loop (bench/bench_formats.cu:183-186)
+    on decoded A [M x K] and FP16 B [K x N]: D [M x N] FP32."""
+    r = ref_lib()
+    if r is None:
+        raise RuntimeError("oracle/_ref was not built (needs the reference checkout at build time)")
+    out = np.empty((M, N), dtype=np.float32)
+    r.ref_naive_decode_gemm(a_fmt, _c(np.ascontiguousarray(A)), _c(np.ascontiguousarray(B16_kn)), _c(out), M, N, K,
+                            float(alpha))
     return out
 
 

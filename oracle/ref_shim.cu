@@ -96,8 +96,12 @@ void ref_cpu_decode_gemm(int a_fmt, const void* A, const uint16_t* B, float* D, 
                          int row1, float alpha, int nthreads) {
     (void)M;
     if (nthreads > 0) omp_set_num_threads(nthreads);
-    float* bf = new float[static_cast<size_t>(N) * K];
-    for (size_t i = 0; i < static_cast<size_t>(N) * K; ++i) bf[i] = __half2float(__ushort_as_half(B[i]));
+    // B is widened once per call, split over the threads like the rows (a
+    // fixed cost that a single thread would make dominate short row samples).
+    const long long nk = static_cast<long long>(N) * K;
+    float* bf = new float[static_cast<size_t>(nk)];
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < nk; ++i) bf[i] = __half2float(__ushort_as_half(B[i]));
 #pragma omp parallel
     {
         float* arow = new float[K];
@@ -114,6 +118,28 @@ void ref_cpu_decode_gemm(int a_fmt, const void* A, const uint16_t* B, float* D, 
         delete[] arow;
     }
     delete[] bf;
+}
+
+/* The reference's own CPU check product (bench/bench_formats.cu:183-186), one
+ * thread: D[i][j] = sum_k a[i][k] * b[k][j] in ascending k with B in its
+ * [K x N] row-major layout, after decoding A [M x K] with the reference
+ * primitives (row by row) and widening B [K x N] FP16 with __half2float.
+ * The naive loop whose timing the build's GPU path is set against at the
+ * sizes where it is tractable (256^3, 512^3). */
+void ref_naive_decode_gemm(int a_fmt, const void* A, const uint16_t* B_kn, float* D, int M, int N, int K,
+                           float alpha) {
+    float* b = new float[static_cast<size_t>(K) * N];
+    for (size_t i = 0; i < static_cast<size_t>(K) * N; ++i) b[i] = __half2float(__ushort_as_half(B_kn[i]));
+    float* a = new float[static_cast<size_t>(M) * K];
+    for (size_t i = 0; i < static_cast<size_t>(M) * K; ++i) a[i] = ref_decode_f32(a_fmt, A, i);
+    for (int i = 0; i < M; ++i)
+        for (int j = 0; j < N; ++j) {
+            float s = 0.0f;
+            for (int k = 0; k < K; ++k) s += a[static_cast<size_t>(i) * K + k] * b[static_cast<size_t>(k) * N + j];
+            D[static_cast<size_t>(i) * N + j] = s * alpha;
+        }
+    delete[] a;
+    delete[] b;
 }
 
 }  // extern "C"

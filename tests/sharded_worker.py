@@ -1,5 +1,5 @@
-"""One rank of the 2-GPU sharded-GEMM test (launched by tests/test_sharded_gpu.py
-through torch.distributed.run).  gloo carries only the NCCL unique id; the
+"""One rank of the multi-GPU sharded-GEMM test (launched by tests/test_sharded_gpu.py
+through torch.distributed.run, two or four ranks).  gloo carries only the NCCL unique id; the
 GEMM's all-gather runs on the library's own NCCL communicator."""
 import datetime
 import os

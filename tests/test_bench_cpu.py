@@ -26,3 +26,41 @@ def test_reference_arm_prints_contract_line():
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert "workload" in line["config"]
+
+
+def _bench_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_reference_arm_config_matches_ours():
+    """Both arms name the same workload object, so the two lines compare."""
+    bench = _bench_module()
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["config"] == bench.sweep_config(4096, 4096, 4096, 1)
+
+
+def test_targets_object_is_compact():
+    """The target figures close the line in a few hundred characters, so they
+    survive in the tail of the output that is kept."""
+    bench = _bench_module()
+    sq = {"pct_f16_dense_peak_nominal": 75.0}
+    mlp = [{"W": w, "fmt": f, "tokens": t, "fused_pct_hbm": 50.0 + t}
+           for w in ("14336x4096", "4096x14336") for f in ("e4m3", "e2m1") for t in (1, 16, 128, 2048)]
+    formats = {k: {"fused_tflops": 1.0, "unfused_tflops": 2.0} for k in bench.FORMATS}
+    formats.update({f"native_{k}": {"pct_fp8_dense_peak": 50.0} for k in ("e4m3", "e2m1")})
+    line = {"fp4_8192_fused": sq, "fp4_8192_fused_after_load": sq, "e4m3_8192_fused": sq, "weight_only_mlp": mlp,
+            "formats": formats, "int8_4096": {"pct_i8_dense_peak": 40.0},
+            "sharded_weight_gemm": {"world": 1, "ms": 9.9, "check": {"pass": True, "rel_frob_max_vs_fp64": 1e-6}},
+            "config_256_e4m3": {"us": 5.0, "rel_frob_vs_unquantized_fp32": 0.025},
+            "cpu_baseline": {"naive_single_thread": {"256^3": {"ms": 15.0}, "512^3": {"ms": 120.0}}}}
+    t = bench.targets(line)
+    assert t["skinny_pct_hbm_min_max"]["14336x4096_e4m3"] == [51.0, 66.0]
+    assert t["sharded"]["check_pass"] is True
+    assert len(json.dumps(t)) < 1200

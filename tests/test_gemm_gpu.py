@@ -411,3 +411,35 @@ def test_fp8_fused_fp16_mirror(tb, cuda):
 
 def test_no_device_error_word(tb, cuda):
     assert tb.device_error(clear=True) == 0
+
+
+def test_quantize_then_narrow_gemm_same_stream(tb, cuda):
+    """tb_quantize writes the weights and a narrow GEMM reads them on the same
+    stream with no host synchronisation, separated as the header asks by one
+    kernel launched without programmatic dependent launch (a fill of another
+    buffer): every result equals, bit for bit, the same GEMM run after a full
+    synchronisation."""
+    M, N, K = 2048, 16, 4096
+    g = cuda.Generator(device="cuda")
+    g.manual_seed(61)
+    ws = [cuda.randn(M, K, generator=g, device="cuda") * 0.02 for _ in range(2)]
+    B = cuda.randn(N, K, generator=g, device="cuda").half()
+    for fmt in (O.E4M3, O.E2M1):
+        A = cuda.empty(tb.stored_bytes(fmt, M * K), dtype=cuda.uint8, device="cuda")
+        want = []
+        for w in ws:
+            tb.quantize(fmt, w, A, M * K, scale=64.0)
+            cuda.cuda.synchronize()
+            D = cuda.empty(M, N, dtype=cuda.float32, device="cuda")
+            tb.gemm_fused(fmt, A, B, D, M, N, K, alpha=1.0 / 64)
+            cuda.cuda.synchronize()
+            want.append(D)
+        outs = [cuda.empty(M, N, dtype=cuda.float32, device="cuda") for _ in range(8)]
+        sep = cuda.empty(1024, dtype=cuda.float32, device="cuda")
+        for i, D in enumerate(outs):
+            tb.quantize(fmt, ws[i & 1], A, M * K, scale=64.0)
+            sep.fill_(float(i))
+            tb.gemm_fused(fmt, A, B, D, M, N, K, alpha=1.0 / 64)
+        cuda.cuda.synchronize()
+        for i, D in enumerate(outs):
+            assert cuda.equal(D.view(cuda.int32), want[i & 1].view(cuda.int32)), (fmt, i)

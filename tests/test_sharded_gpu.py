@@ -1,7 +1,8 @@
-"""Column-sharded fused GEMM over NCCL on two GPUs: every rank ends with the
-whole D, bit-identical to the single-GPU fused GEMM (each row block is computed
-by the same kernel with the same K order) and within 1e-3 relative Frobenius
-error of the oracle.  Needs two GPUs; skipped on one."""
+"""Column-sharded fused GEMM over NCCL on two and four GPUs: every rank ends
+with the whole D, bit-identical to the single-GPU fused GEMM (each row block is
+computed by the same kernel with the same K order) and within 1e-3 relative
+Frobenius error of the oracle.  Each world size needs that many GPUs and is
+skipped with fewer."""
 import os
 import socket
 import subprocess
@@ -20,13 +21,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_sharded_fused_two_gpus(cuda):
-    if cuda.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_fused(cuda, world):
+    if cuda.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", NCCL_DEBUG="WARN")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(ROOT, "tests", "sharded_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "rank 0 OK" in r.stdout and "rank 1 OK" in r.stdout
+    for rank in range(world):
+        assert f"rank {rank} OK" in r.stdout, r.stdout[-3000:]
