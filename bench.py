@@ -589,6 +589,25 @@ def fused_square(torch, tb, peaks, fmt_name: str = "e2m1", n: int = 8192, iters:
             "frac_of_measured_bf16": tf / peaks["bf16_tflops"], "clocks": clk}
 
 
+def nvfp4_square(torch, tb, n: int = 8192, iters: int = 20):
+    """Block-scaled FP4 with both operands quantized (packed E2M1 codes, one
+    UE4M3 scale byte per 16 values) at n^3 on tcgen05 kind::mxf4nvf4, FP16
+    out; codes uniform over all 16 values, scale bytes uniform in 0x30-0x47.
+    Dense FP4 peak 9 PFLOP/s nominal."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(94)
+    A = torch.randint(0, 256, (n, n // 2), generator=g, device="cuda", dtype=torch.uint8)
+    B = torch.randint(0, 256, (n, n // 2), generator=g, device="cuda", dtype=torch.uint8)
+    SA = torch.randint(0x30, 0x48, (n, n // 16), generator=g, device="cuda", dtype=torch.uint8)
+    SB = torch.randint(0x30, 0x48, (n, n // 16), generator=g, device="cuda", dtype=torch.uint8)
+    D = torch.empty(n, n, dtype=torch.float16, device="cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    ms = time_each(torch, lambda: tb.gemm_nvfp4(A, SA, B, SB, D, n, n, n, out=tb.Out.F16, alpha=1e-4), iters, flush)
+    tf = 2.0 * n ** 3 / ms / 1e9
+    return {"M": n, "N": n, "K": n, "out": "f16", "ms": ms, "tflops": tf, "pct_fp4_dense_peak_nominal": 100 * tf / 9000.0,
+            "pct_fp8_dense_peak_nominal": 100 * tf / 4500.0}
+
+
 def config_256(torch, tb, iters: int = 50):
     """The 256 x 256 x 256 FP8 E4M3 weight-only GEMM: A from U[-1, 1] (seed 0)
     quantized with scale 448/maxabs, B from U[-1, 1] (seed 1) in FP16; fused
@@ -1015,6 +1034,8 @@ def main():
         torch.cuda.empty_cache()
         line["config_256_e4m3"] = config_256(torch, tb)
         torch.cuda.empty_cache()
+        line["nvfp4_8192"] = nvfp4_square(torch, tb)
+        torch.cuda.empty_cache()
         line["decode_stream_14336x4096"] = decode_streams(torch, tb, peaks)
         torch.cuda.empty_cache()
         line["weight_only_mlp"] = mlp_weight_only(torch, tb, peaks)
@@ -1055,6 +1076,9 @@ def targets(line: dict) -> dict:
     fm = line["formats"]
     t["fused_ge_unfused_4096"] = {k: fm[k]["fused_tflops"] >= fm[k]["unfused_tflops"] for k in FORMATS}
     t["native_pct_fp8_dense"] = {k: r(fm[f"native_{k}"]["pct_fp8_dense_peak"]) for k in ("e4m3", "e2m1")}
+    nv = line.get("nvfp4_8192")
+    if nv:
+        t["nvfp4_8192"] = {"tflops": r(nv["tflops"], 0), "pct_fp4_dense": r(nv["pct_fp4_dense_peak_nominal"])}
     t["int8_pct_i8_dense"] = r(line["int8_4096"]["pct_i8_dense_peak"])
     sh = line["sharded_weight_gemm"]
     t["sharded"] = {"world": sh["world"], "ms": r(sh["ms"], 3), "check_pass": sh["check"]["pass"],

@@ -223,6 +223,25 @@ tb_status tb_gemm_fused_noalloc(tb_format a_fmt, const void* A, const uint16_t* 
 tb_status tb_gemm_native(tb_format a_fmt, const void* A, tb_format b_fmt, const void* B, void* D,
                          int M, int N, int K, tb_out_type out, float alpha, tb_stream_t stream);
 
+/* Block-scaled FP4 with both operands quantized (the NVFP4 layout that
+ * fp4.h:6 names and docs/quantization-limits.md:14-33 argues for; the
+ * reference has no kernel for it), run natively by tcgen05.mma
+ * kind::mxf4nvf4.block_scale on pairs of SMs at the FP4 tensor rate:
+ *   D[M x N] = alpha * (A .* SA) * (B .* SB)^T
+ * A [M x K] and B [N x K] hold E2M1 codes packed two per byte with the FIRST
+ * value in the LOW nibble (TB_FMT_E2M1_HW order; tb_fp4_repack_hw converts
+ * reference-packed codes); SA [M x K/16] and SB [N x K/16] hold one scale
+ * byte per 16 consecutive values of a row, row-major.  Scale bytes are
+ * UE4M3: E4M3 with the sign bit clear, 0x00-0x7E (0x7F is NaN); a byte with
+ * the sign bit set is outside this call's contract (tb_decode_nvfp4 accepts
+ * every byte).  alpha carries the per-tensor FP32 scales (for two-level
+ * quantization x = decode * g, alpha = gA * gB).  K % 256 == 0; all four
+ * arrays 16-byte aligned; any M, N >= 1.  FP32 accumulation; FP32 or FP16
+ * out.  Results equal, within FP32 accumulation error, the FP16 GEMM of the
+ * operands decoded by tb_decode_nvfp4 (whose products are exact). */
+tb_status tb_gemm_nvfp4(const uint8_t* A, const uint8_t* A_scales, const uint8_t* B, const uint8_t* B_scales, void* D,
+                        int M, int N, int K, tb_out_type out, float alpha, tb_stream_t stream);
+
 /* Swap the two nibbles of every byte: reference FP4 packing (first value high)
  * <-> tensor-core packing (first value low).  n_bytes bytes, may be in place. */
 tb_status tb_fp4_repack_hw(const uint8_t* src, uint8_t* dst, size_t n_bytes, tb_stream_t stream);

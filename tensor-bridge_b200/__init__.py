@@ -97,6 +97,7 @@ SIGNATURES = {
     "tb_gemm_fused_workspace": (_sz, [_i, _i, _i, _i]),
     "tb_gemm_fused_noalloc": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p]),
     "tb_gemm_native": (_st, [_i, _p, _i, _p, _p, _i, _i, _i, _i, _f, _p]),
+    "tb_gemm_nvfp4": (_st, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _f, _p]),
     "tb_fp4_repack_hw": (_st, [_p, _p, _sz, _p]),
     "tb_gemm_fp8_fused_fp16": (_st, [_p, _p, _p, _i, _i, _i, _p, _sz, _p]),
     "tb_gemm_fp8_fused_workspace": (_sz, [_i, _i, _i]),
@@ -210,6 +211,13 @@ def gemm_fused_noalloc(fmt, A, B, D, M: int, N: int, K: int, out=Out.F32, alpha:
 
 def gemm_native(a_fmt, A, b_fmt, B, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):
     call("tb_gemm_native", int(a_fmt), _ptr(A), int(b_fmt), _ptr(B), _ptr(D), M, N, K, int(out), alpha,
+         _stream(stream))
+
+
+def gemm_nvfp4(A, A_scales, B, B_scales, D, M: int, N: int, K: int, out=Out.F32, alpha: float = 1.0, stream=None):
+    """Block-scaled FP4 GEMM: codes in the tensor-core nibble order (E2M1_HW),
+    one UE4M3 scale byte per 16 values of a row (tcgen05 kind::mxf4nvf4)."""
+    call("tb_gemm_nvfp4", _ptr(A), _ptr(A_scales), _ptr(B), _ptr(B_scales), _ptr(D), M, N, K, int(out), alpha,
          _stream(stream))
 
 

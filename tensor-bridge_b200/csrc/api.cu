@@ -254,6 +254,24 @@ tb_status tb_gemm_fused(tb_format a_fmt, const void* A, const uint16_t* B, void*
     return fused_request(a_fmt, A, B, D, N, M, N, K, out, alpha, workspace, workspace_bytes, stream);
 }
 
+tb_status tb_gemm_nvfp4(const uint8_t* A, const uint8_t* A_scales, const uint8_t* B, const uint8_t* B_scales, void* D,
+                        int M, int N, int K, tb_out_type out, float alpha, tb_stream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0) return fail(TB_ERR_SHAPE, "M, N, K must be positive (got %d, %d, %d)", M, N, K);
+    if (K % 256 != 0) return fail(TB_ERR_SHAPE, "K = %d must be a multiple of 256 for the block-scaled FP4 GEMM", K);
+    if (!A || !A_scales || !B || !B_scales || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
+    if (out != TB_OUT_F32 && out != TB_OUT_F16) return fail(TB_ERR_INVALID_ARGUMENT, "bad output type");
+    if (!aligned16(A) || !aligned16(B) || !aligned16(A_scales) || !aligned16(B_scales))
+        return fail(TB_ERR_ALIGNMENT, "A, B and both scale arrays must be 16-byte aligned");
+    tb_status s = check_device();
+    if (s != TB_OK) return s;
+    const char* why = nullptr;
+    cudaError_t e = tb::nvfp4_gemm_launch(A, A_scales, B, B_scales, D, M, N, K, out == TB_OUT_F16, alpha,
+                                          reinterpret_cast<cudaStream_t>(stream), &why);
+    if (e == cudaSuccess) return TB_OK;
+    if (why) return fail(TB_ERR_UNSUPPORTED, "%s", why);
+    return fail(TB_ERR_LAUNCH, "block-scaled FP4 GEMM launch: %s", cudaGetErrorString(e));
+}
+
 tb_status tb_gemm_native(tb_format a_fmt, const void* A, tb_format b_fmt, const void* B, void* D, int M, int N, int K,
                          tb_out_type out, float alpha, tb_stream_t stream) {
     auto native_ok = [](tb_format f) { return f == TB_FMT_E4M3 || f == TB_FMT_E5M2 || f == TB_FMT_E2M1_HW; };

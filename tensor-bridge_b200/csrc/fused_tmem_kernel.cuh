@@ -10,16 +10,19 @@
 // TMEM (tcgen05.mma ... [a_tmem], b_desc), so shared memory carries only the
 // raw weights and the small B tiles.
 //
-// Everything is organised in rounds of four k-blocks (256 values of K).  On
-// sm_100a an mbarrier wait or arrive costs on the order of 150 cycles of
-// latency even when it does not block, and one M = 128, K = 16 MMA occupies
-// the tensor pipe for about 40 cycles whatever BN is, so the k-block loop is
-// bounded by how many barrier operations sit on each role's path.  Per round
-// the MMA issuer waits once (rdy) and commits once (fre).  The decode warps
-// touch no mbarrier at all: a sync warp does their waits one round ahead
-// (raw stages landed, TMEM stages freed) and their arrivals (raw stages
-// consumed, round decoded), and hands rounds to them through two pairs of
-// hardware named barriers, which cost a few tens of cycles.
+// Everything is organised in rounds of four k-blocks (256 values of K): per
+// round the MMA issuer waits once (rdy) and commits once (fre).  On sm_100a an
+// mbarrier wait or arrive costs on the order of 150 cycles of latency even
+// when it does not block, while an M = 128, N = 16, K = 16 MMA with A in
+// tensor memory occupies the tensor pipe for about 9 cycles, so the schedule
+// is set by how many barrier operations sit on each role's path per round.
+// The decode warps form NG groups of eight (two per TMEM lane quarter, each
+// decoding two of the round's four k-blocks); group g decodes whole rounds
+// r = g, g + NG, ... and does its own waits (the
+// round's TMEM slot freed, its raw stages landed) and arrivals (raw stages
+// consumed, round in TMEM), so NG rounds are decoded at once and a round's
+// barrier latency is paid once per group, not once per round on a shared
+// path.
 //
 // Roles (one persistent CTA per SM, same work units as gemm_kernel.cuh):
 //   warp 0      TMA producer of the raw A ring.  A raw stage holds RSK
@@ -28,50 +31,59 @@
 //               spans SPR = 4 / RSK stages.
 //   warp 1      TMEM allocator (all 512 columns) and MMA issuer
 //   warps 2-5   epilogue (as in gemm_kernel.cuh)
-//   warps 6-21  16 decode warps.  A warp may only touch the 32 TMEM lanes of
+//   warps 6-    decode warps.  A warp may only touch the 32 TMEM lanes of
 //               its warp-id quarter q = warp % 4, so thread i owns tile row
-//               32 q + i.  Slice j = (warp - 6) / 4 of a quarter decodes
-//               k-block j of every round, whole rows of 64 values.
-//   warp 22     TMA producer of the B tiles: one per k-block of a round
-//   warp 23     sync warp of the decode warps
+//               32 q + i.  Group mode: NG = NRND groups of eight warps;
+//               warp i = (warp - 6) % 8 of group g = (warp - 6) / 8 decodes
+//               k-blocks 2 (i / 4) and 2 (i / 4) + 1 of its rounds (the
+//               decode is issue-bound: the second warp per quarter hides
+//               latency the first cannot).
+//               Per-warp mode (TF32, whose 128 KB rounds leave a raw ring of
+//               one round): sixteen warps, slice j = (warp - 6) / 4 decodes
+//               k-block j of every round and waits and arrives itself.
+//   last warp   TMA producer of the B tiles into their own ring of NBR round
+//               slots (one tile per k-block), as far ahead of the MMAs as the
+//               ring allows: B is the same for every CTA and usually in L2,
+//               but under full HBM load a TMA round trip takes 1-1.5 us,
+//               which would otherwise sit in every TMEM slot's reuse cycle
 // TMEM columns: [0, 2 BN) two accumulators, then from column max(128, 2 BN)
 // NRND round slots (3 for BN <= 32; 2 for BN = 64, where the B tiles are
 // larger, and for BN = 128, where TMEM holds no more) of four A stages of 32
 // columns (64 FP16 values of K per lane).
 //
 // Barriers, all waits bounded:
-//   raw_full / raw_empty  per raw slot: TMA bytes / the sync warp's arrival
-//                         once the decode warps have read the stage.
-//   rdy[r % NRND]         round r is ready: the sync warp's arrival (the decode
-//                         warps' tcgen05.st has completed) and the B
-//                         producer's arrival with the round's B bytes.
+//   raw_full / raw_empty  per raw slot: TMA bytes / the arrivals of the
+//                         decode warps that read the stage.
+//   rdy[r % NRND]         round r is in TMEM: the decode warps' arrivals (their
+//                         tcgen05.st has completed).
 //   fre[r % NRND]         round r's MMAs have completed (one commit): its TMEM
-//                         stages and B tiles may be overwritten.
+//                         stages may be overwritten.
+//   b_full / b_empty      per B round slot: TMA bytes / the commit of the
+//                         round's MMAs.
 //   acc_full / acc_empty  as in gemm_kernel.cuh.
-//   named START[r % 2]    the sync warp arrives once round r's raw stages have
-//                         landed and its TMEM stages are free; the 16 decode
-//                         warps wait.
-//   named DONE[r % 2]     the decode warps arrive once round r is in TMEM and
-//                         its raw words are consumed; the sync warp waits.
-// Every role takes part in every round, including the short last round of a
-// unit, so each waiter has seen the previous phase of every barrier it waits
-// on and a parity wait cannot pass on a stale phase.  The named barriers have
-// no timeout, so the sync warp and the decode warps go through all of them
-// for every round even after an abort (they then skip the waits and the work).
+// A parity wait passes on a stale phase if the barrier is two phases behind
+// the one waited for.  The MMA issuer, the producers and the per-warp decode
+// warps walk every round in order, so they cannot be.  A decode group walks
+// only its own rounds; it waits for its round's TMEM slot first (fre of round
+// r - NRND, which its own previous wait, for round r - NG, kept from being two
+// phases behind because NG <= NRND) and for the raw stages after that: the
+// MMAs of round r - NRND imply that every earlier round was decoded, so the
+// previous fill of each of its raw slots (round r - SR / SPR, with
+// SR / SPR >= NRND) has landed.  tests/test_ring_protocol.py models both
+// modes under random schedules and shows the failures these conditions rule
+// out.
 #pragma once
 
 #include "gemm_kernel.cuh"
 
 namespace tb {
 
-template <int BN_, int FMT_, int SR_, int NRND_>
+template <int BN_, int FMT_, int SR_, int NRND_, int NBR_>
 struct TmemCfg {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
     static constexpr int FMT = FMT_;
     static constexpr int DK = 4;                          // k-blocks per round
-    static constexpr int NSLICE = 4;                      // decode warps per TMEM lane quarter
-    static constexpr int ND = 4 * NSLICE;
     static constexpr int ROW_BYTES = raw_row_bytes(FMT);  // raw bytes of one k-block row
     static constexpr int RSK = ROW_BYTES <= 64 ? 4 : ROW_BYTES == 128 ? 2 : 1;  // k-blocks per raw stage
     static constexpr int SPR = DK / RSK;                  // raw stages per round
@@ -83,21 +95,20 @@ struct TmemCfg {
     // because HBM serves the requests of all CTAs interleaved; a bounded
     // number in flight lands in order and the first round arrives early.
     // The stage waited for must not have been refilled yet: INFLIGHT < SR.
-    static constexpr int INFLIGHT0 = (96 * 1024) / STAGE_BYTES < 1 ? 1 : (96 * 1024) / STAGE_BYTES;
-    static constexpr int INFLIGHT = INFLIGHT0 < SR - 1 ? INFLIGHT0 : SR - 1;
+    static constexpr int INFLIGHT = SR - 1;
     static constexpr int NRND = NRND_;                    // round slots (TMEM A stages, B tiles)
     static constexpr int B_BYTES = BN * 128;              // one k-block of B
+    static constexpr int NBR = NBR_;                      // B ring slots (rounds)
+    // Group mode when the raw ring holds at least NRND rounds (every format
+    // but TF32); NG = NRND groups of GW = 8 decode warps.
+    static constexpr bool GROUPS = SR / SPR >= NRND;
+    static constexpr int NG = GROUPS ? NRND : 0;
+    static constexpr int GW = 8;
+    static constexpr int ND = GROUPS ? GW * NG : 16;      // decode warps
     static constexpr int DECODE_WARP0 = 6;
     static constexpr int B_WARP = DECODE_WARP0 + ND;
-    static constexpr int SYNC_WARP = B_WARP + 1;
-    static constexpr int NUM_THREADS = (SYNC_WARP + 1) * 32;
-    // The sync warp hands whole rounds to the decode warps when the raw ring
-    // holds at least two rounds (all formats but TF32, whose 128 KB rounds
-    // do not fit twice); otherwise each decode warp waits and arrives itself.
-    static constexpr bool SYNCW = SR >= 2 * SPR;
-    // Named barriers (0 is __syncthreads): START 1-2, DONE 3-4.
-    static constexpr uint32_t NB_START = 1, NB_DONE = 3, NB_COUNT = (ND + 1) * 32;
-    static constexpr uint32_t NB_SETUP = 5;  // set-up: warp 0 arrives, the others wait
+    static constexpr int NUM_THREADS = (B_WARP + 1) * 32;
+    static constexpr uint32_t NB_SETUP = 1;  // set-up named barrier: warp 0 arrives, the others wait
 
     static constexpr int A_COL0 = 2 * BN > 128 ? 2 * BN : 128;
     static constexpr int TMEM_COLS = 512;
@@ -113,8 +124,8 @@ struct TmemCfg {
 
     static constexpr int OFF_R = 0;
     static constexpr int OFF_B = OFF_R + SR * STAGE_BYTES;
-    static constexpr int OFF_BAR = OFF_B + NRND * DK * B_BYTES;
-    static constexpr int NUM_BARS = 2 * SR + 2 * NRND + 5;
+    static constexpr int OFF_BAR = OFF_B + NBR * DK * B_BYTES;
+    static constexpr int NUM_BARS = 2 * SR + 2 * NRND + 2 * NBR + 5;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
 
@@ -125,6 +136,8 @@ struct TmemCfg {
     static_assert(WPH == 32 || WPH == 16, "TMEM store width");
     static_assert(2 * BN <= A_COL0 && A_COL0 + NRND * DK * 32 <= TMEM_COLS && NRND >= 2, "TMEM budget");
     static_assert(SR % SPR == 0 && SR >= SPR, "each raw slot holds one stage position of a round");
+    static_assert(!GROUPS || (NG <= NRND && SR / SPR >= NRND), "group mode parity conditions");
+    static_assert(NUM_THREADS <= 1024, "block size");
     static_assert(B_BYTES % 1024 == 0, "B tile alignment");
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
@@ -196,7 +209,8 @@ __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, 
 template <int FMT>
 __device__ __forceinline__ uint32_t unit_special_mask(const uint4& in) {
     if constexpr (FMT == kE4M3)
-        return e4m3_special_mask(in.x) | e4m3_special_mask(in.y) | e4m3_special_mask(in.z) | e4m3_special_mask(in.w);
+        return (e4m3_special_bits(in.x) | e4m3_special_bits(in.y) | e4m3_special_bits(in.z) | e4m3_special_bits(in.w)) &
+               0x80808080u;
     else if constexpr (FMT == kBF16)
         return bf16_nan_lanes(in.x) | bf16_nan_lanes(in.y) | bf16_nan_lanes(in.z) | bf16_nan_lanes(in.w);
     else if constexpr (FMT == kTF32)
@@ -265,7 +279,9 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     uint64_t* raw_empty = raw_full + C::SR;
     uint64_t* rdy = raw_empty + C::SR;
     uint64_t* fre = rdy + C::NRND;
-    uint64_t* acc_full = fre + C::NRND;
+    uint64_t* b_full = fre + C::NRND;
+    uint64_t* b_empty = b_full + C::NBR;
+    uint64_t* acc_full = b_empty + C::NBR;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* fin_bar = acc_empty + 2;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(fin_bar + 1);
@@ -277,11 +293,15 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::SR; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], C::SYNCW ? 1 : 4 * C::RSK);
+            mbar_init(&raw_empty[s], C::GROUPS ? C::GW : 4 * C::RSK);
         }
         for (int s = 0; s < C::NRND; ++s) {
-            mbar_init(&rdy[s], C::SYNCW ? 2 : C::ND + 1);
+            mbar_init(&rdy[s], C::GROUPS ? C::GW : C::ND);
             mbar_init(&fre[s], 1);
+        }
+        for (int s = 0; s < C::NBR; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
@@ -378,13 +398,13 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             const int tn = x.tn, kb0 = x.kb0, kb1 = x.kb1;
             for (int kb = kb0; kb < kb1; kb += C::DK, ++r) {
                 const int cnt = min(C::DK, kb1 - kb);
-                const uint32_t slot = r % C::NRND, use = r / C::NRND;
-                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&fre[slot], (use & 1u) ^ 1u, abort_flag))) { ok = false; break; }
+                const uint32_t bs = r % C::NBR, buse = r / C::NBR;
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&b_empty[bs], (buse & 1u) ^ 1u, abort_flag))) { ok = false; break; }
                 if (elect_one()) {
-                    mbar_arrive_expect_tx(&rdy[slot], static_cast<uint32_t>(cnt * C::B_BYTES));
-                    uint8_t* dst = smem + C::OFF_B + slot * (C::DK * C::B_BYTES);
+                    mbar_arrive_expect_tx(&b_full[bs], static_cast<uint32_t>(cnt * C::B_BYTES));
+                    uint8_t* dst = smem + C::OFF_B + bs * (C::DK * C::B_BYTES);
                     for (int d = 0; d < cnt; ++d)
-                        tma_load_2d(dst + d * C::B_BYTES, &tmB, &rdy[slot], (kb + d) * 64, tn * C::BN);
+                        tma_load_2d(dst + d * C::B_BYTES, &tmB, &b_full[bs], (kb + d) * 64, tn * C::BN);
                 }
                 __syncwarp();
             }
@@ -408,10 +428,12 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             for (int kb = kb0; kb < kb1; kb += C::DK, ++r) {
                 const int cnt = min(C::DK, kb1 - kb);
                 const uint32_t slot = r % C::NRND, use = r / C::NRND;
+                const uint32_t bs = r % C::NBR, buse = r / C::NBR;
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait(&b_full[bs], buse & 1u, abort_flag))) { ok = false; break; }
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&rdy[slot], use & 1u, abort_flag))) { ok = false; break; }
                 tc_fence_after();
                 if (elect_one()) {
-                    const uint32_t b_lo = sdesc_lo(sbase + C::OFF_B + slot * (C::DK * C::B_BYTES));
+                    const uint32_t b_lo = sdesc_lo(sbase + C::OFF_B + bs * (C::DK * C::B_BYTES));
                     const uint32_t a_t = tmem_base + static_cast<uint32_t>(C::A_COL0 + slot * C::DK * 32);
 #pragma unroll
                     for (int d = 0; d < C::DK; ++d) {
@@ -426,6 +448,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                         }
                     }
                     mma_commit(&fre[slot]);
+                    mma_commit(&b_empty[bs]);
                 }
                 __syncwarp();
             }
@@ -467,82 +490,57 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
         }
-    } else if (warp == C::SYNC_WARP) {
-        // ---------------- sync warp: the decode warps' mbarrier traffic, one round ahead ----------------
-        if constexpr (C::SYNCW) {
-            uint32_t nr = 0;  // rounds of this CTA
-            {
-                NCursor cur;
-                ncur_init(p, cur);
-                NUnit x;
-                while (ncur_next(p, cur, x)) nr += static_cast<uint32_t>((x.kb1 - x.kb0 + C::DK - 1) / C::DK);
-            }
-            bool ok = true;
-            // Round r's raw stages have landed and its TMEM stages are free.
-            auto ready = [&](uint32_t r) -> bool {
-                bool good = true;
-#pragma unroll 1
-                for (int pos = 0; pos < C::SPR && good; ++pos) {
-                    const uint32_t st = r * C::SPR + pos;
-                    good = __all_sync(0xFFFFFFFFu, mbar_wait(&raw_full[st % C::SR], (st / C::SR) & 1u, abort_flag));
-                }
-                const uint32_t use = r / C::NRND;
-                return good && __all_sync(0xFFFFFFFFu, mbar_wait(&fre[r % C::NRND], (use & 1u) ^ 1u, abort_flag));
-            };
-            if (nr > 0) {
-                ok = ready(0);
-                named_bar_arrive(C::NB_START, C::NB_COUNT);
-            }
-            for (uint32_t r = 0; r < nr; ++r) {
-                // Open round r + 1 as soon as it is ready, so a decode warp that
-                // finishes round r early goes on without waiting for the others.
-                // START[(r + 1) % 2] last served round r - 1, which every decode
-                // warp passed before the DONE of round r - 1 that this warp has
-                // already waited for.
-                if (r + 1 < nr) {
-                    if (ok) ok = ready(r + 1);
-                    named_bar_arrive(C::NB_START + ((r + 1) & 1u), C::NB_COUNT);
-                }
-                named_bar_sync(C::NB_DONE + (r & 1u), C::NB_COUNT);
-                if (ok && lane == 0) {
-#pragma unroll 1
-                    for (int pos = 0; pos < C::SPR; ++pos) mbar_arrive(&raw_empty[(r * C::SPR + pos) % C::SR]);
-                    mbar_arrive(&rdy[r % C::NRND]);
-                }
-                __syncwarp();
-            }
-        }
     } else if (warp < C::B_WARP) {
-        // ---------------- decode warps: k-block j of each round -> FP16 words -> TMEM ----------------
+        // ---------------- decode warps: raw stages -> FP16 words -> TMEM ----------------
         const int q = warp & 3;                          // TMEM lane quarter
-        const int j = (warp - C::DECODE_WARP0) >> 2;     // slice: k-block j of every round
         const int row = q * 32 + lane;                   // tile row owned by this thread
-        const int pos = j / C::RSK, sub = j % C::RSK;    // raw stage of the round, k-block within it
-        const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                static_cast<uint32_t>(C::A_COL0 + j * 32);
+        const uint32_t t_quarter = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(C::A_COL0);
         uint32_t r = 0;
-        if constexpr (C::SYNCW) {
+        if constexpr (C::GROUPS) {
+            // Group g decodes rounds g, g + NG, ...; this warp k-blocks d0 and d0 + 1 of each.
+            const uint32_t g = static_cast<uint32_t>((warp - C::DECODE_WARP0) / C::GW);
+            const int d0 = 2 * (((warp - C::DECODE_WARP0) % C::GW) >> 2);
+            bool ok = true;
             NCursor cur;
             ncur_init(p, cur);
             NUnit x;
-            while (ncur_next(p, cur, x)) {
+            while (ok && ncur_next(p, cur, x)) {
                 const int kb0 = x.kb0, kb1 = x.kb1;
                 for (int kb = kb0; kb < kb1; kb += C::DK, ++r) {
-                    named_bar_sync(C::NB_START + (r & 1u), C::NB_COUNT);
-                    // The short last round of a unit; nothing after an abort.
-                    const bool mine = j < kb1 - kb && *abort_flag == 0;
-                    tc_fence_after();
-                    if (mine) {
+                    if (r % C::NG != g) continue;
+                    const int cnt = min(C::DK, kb1 - kb);  // the short last round of a unit
+                    const uint32_t slot = r % C::NRND, use = r / C::NRND;
+                    // The round's TMEM slot first, then its raw stages (see the parity note above).
+                    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&fre[slot], (use & 1u) ^ 1u, abort_flag))) { ok = false; break; }
+#pragma unroll 1
+                    for (int pos = 0; ok && pos < C::SPR; ++pos) {
                         const uint32_t st = r * C::SPR + pos;
-                        decode_kblock<C>(sbase + C::OFF_R + (st % C::SR) * C::STAGE_BYTES, sub, row,
-                                         t_lane + static_cast<uint32_t>((r % C::NRND) * C::DK * 32));
-                        tmem_wait_st();
+                        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&raw_full[st % C::SR], (st / C::SR) & 1u, abort_flag));
                     }
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t t_slot = t_quarter + slot * (C::DK * 32);
+#pragma unroll 1
+                    for (int d = d0; d < d0 + 2 && d < cnt; ++d) {
+                        const uint32_t st = r * C::SPR + d / C::RSK;
+                        decode_kblock<C>(sbase + C::OFF_R + (st % C::SR) * C::STAGE_BYTES, d % C::RSK, row,
+                                         t_slot + static_cast<uint32_t>(d * 32));
+                    }
+                    tmem_wait_st();
                     tc_fence_before();
-                    named_bar_arrive(C::NB_DONE + (r & 1u), C::NB_COUNT);
+                    __syncwarp();
+                    if (lane == 0) {
+#pragma unroll 1
+                        for (int pos = 0; pos < C::SPR; ++pos) mbar_arrive(&raw_empty[(r * C::SPR + pos) % C::SR]);
+                        mbar_arrive(&rdy[slot]);
+                    }
                 }
             }
         } else {
+            // Per-warp mode: slice j decodes k-block j of every round.
+            const int j = (warp - C::DECODE_WARP0) >> 2;
+            const int pos = j / C::RSK, sub = j % C::RSK;   // raw stage of the round, k-block within it
+            const uint32_t t_lane = t_quarter + static_cast<uint32_t>(j * 32);
             bool ok = true;
             NCursor cur;
             ncur_init(p, cur);

@@ -9,6 +9,7 @@
 #include "fused_pair_kernel.cuh"
 #include "fused_tmem_kernel.cuh"
 #include "gemm_pair_kernel.cuh"
+#include "gemm_nvfp4_kernel.cuh"
 #include "gemm_kernel.cuh"
 #include "tb_host.h"
 
@@ -401,19 +402,26 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
 }
 
 // Narrow fused tiles: decoded A goes to TMEM (fused_tmem_kernel.cuh).  The B
-// ring gets 16 (BN = 16) or 8 slots; the raw ring as many raw A boxes as fit
-// in the rest, up to twelve.
+// ring gets about 64 KB (two to eight rounds), less if the raw ring would
+// otherwise hold fewer than NRND rounds (the decode groups' condition); the
+// raw ring the rest, up to twelve stages.
 template <int BN, int FMT>
 struct PickTmem {
-    static constexpr int NRND = BN <= 32 ? 3 : 2;  // round slots of B tiles and TMEM A stages
+    static constexpr int NRND = BN <= 32 ? 3 : 2;  // round slots of TMEM A stages
     static constexpr int ROW = raw_row_bytes(FMT);
     static constexpr int RSK = ROW <= 64 ? 4 : ROW == 128 ? 2 : 1;
     static constexpr int SPR = 4 / RSK;
     static constexpr int STAGE = RSK * ROW * 128;
-    static constexpr int SR0 = (kSmemBudget - 1024 - NRND * 4 * BN * 128) / STAGE;
+    static constexpr int BROUND = 4 * BN * 128;
+    static constexpr int AVAIL = kSmemBudget - 1024;
+    static constexpr int NBR_T0 = 65536 / BROUND;
+    static constexpr int NBR_T = NBR_T0 > 8 ? 8 : (NBR_T0 < 2 ? 2 : NBR_T0);
+    static constexpr int NBR_G = (AVAIL - NRND * SPR * STAGE) / BROUND;  // most B rounds group mode allows
+    static constexpr int NBR = NBR_G >= 2 && NBR_G < NBR_T ? NBR_G : NBR_T;
+    static constexpr int SR0 = (AVAIL - NBR * BROUND) / STAGE;
     static constexpr int SR1 = SR0 > 12 ? 12 : SR0;
     static constexpr int SR = SR1 / SPR * SPR;
-    using Cfg = TmemCfg<BN, FMT, SR, NRND>;
+    using Cfg = TmemCfg<BN, FMT, SR, NRND, NBR>;
 };
 
 template <int BN, int FMT>
@@ -468,6 +476,59 @@ static cudaError_t run_bn(int bn, const GemmRequest& r, const GemmArgs& a, cudaS
         case 256: return run<256, MODE, FMT>(r, a, st, dev, why);
         default: *why = "unsupported tile width"; return cudaErrorInvalidValue;
     }
+}
+
+// ---- block-scaled FP4 (kind::mxf4nvf4) on SM pairs --------------------------------------
+
+using Nvfp4Of = Nvfp4Cfg<5>;
+
+cudaError_t nvfp4_gemm_launch(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, void* D, int M,
+                              int N, int K, int out_f16, float alpha, cudaStream_t st, const char** why) {
+    using C = Nvfp4Of;
+    const int dev = current_device();
+    const int clusters = cluster_capacity<C>(k_gemm_nvfp4<C>, dev);
+    if (clusters <= 0) {
+        *why = "no room for a two-CTA cluster of the block-scaled FP4 kernel";
+        return cudaErrorInvalidConfiguration;
+    }
+    CUtensorMap ta, tbm, tsa, tsb;
+    const uint64_t kb = static_cast<uint64_t>(K) / 2;   // code bytes per row
+    const uint64_t ks = static_cast<uint64_t>(K) / 16;  // scale bytes per row
+    if (!make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, kb, M, kb, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tbm, CU_TENSOR_MAP_DATA_TYPE_UINT8, B, kb, N, kb, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, sfa, ks, M, ks, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, sfb, ks, N, ks, 16, 256, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+        *why = "cuTensorMapEncodeTiled rejected the operand layout";
+        return cudaErrorInvalidValue;
+    }
+    GemmArgs a{};
+    a.M = M; a.N = N; a.K = K;
+    a.tiles_m = (M + C::BM - 1) / C::BM;
+    a.tiles_n = (N + C::BN - 1) / C::BN;
+    a.splits = 1;
+    a.num_kb = K / C::KB_VALUES;
+    a.kb_per_split = a.num_kb;
+    a.num_units = a.tiles_m * a.tiles_n;
+    a.half_from = a.num_units;
+    a.pair_full = a.num_units;
+    a.alpha = alpha;
+    a.D = D; a.ldd = N;
+    a.out_f16 = out_f16;
+    const int vec_elems = out_f16 ? 8 : 4;
+    a.vec_ok = ((reinterpret_cast<uintptr_t>(D) & 15u) == 0 && (N % vec_elems) == 0) ? 1 : 0;
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * std::min(a.num_units, clusters), 1, 1);
+    cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+    cfg.stream = st;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_gemm_nvfp4<C>, ta, tbm, tsa, tsb, a);
 }
 
 cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why) {

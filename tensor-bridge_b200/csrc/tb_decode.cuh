@@ -46,11 +46,12 @@ __device__ __forceinline__ uint32_t pack2(uint16_t lo, uint16_t hi) {
 // reference encodes as sign | 0x7E00).  With m = code & 0x7F (no byte carries
 // out of its lane): m + 0x7F has bit 7 iff m >= 1;  m + 0x78 iff m >= 8;
 // m + 0x01 iff m == 0x7F.
-__device__ __forceinline__ uint32_t e4m3_special_mask(uint32_t w) {
+__device__ __forceinline__ uint32_t e4m3_special_bits(uint32_t w) {
     const uint32_t m = w & 0x7F7F7F7Fu;
     const uint32_t ge1 = m + 0x7F7F7F7Fu, ge8 = m + 0x78787878u, nan = m + 0x01010101u;
-    return ((ge1 & ~ge8) | nan) & 0x80808080u;
+    return (ge1 & ~ge8) | nan;  // only bit 7 of each byte is meaningful
 }
+__device__ __forceinline__ uint32_t e4m3_special_mask(uint32_t w) { return e4m3_special_bits(w) & 0x80808080u; }
 
 // Bit 7 of each byte set where the code is a NaN (magnitude 0x7F).
 __device__ __forceinline__ uint32_t e4m3_nan_bits(uint32_t w) {

@@ -51,6 +51,10 @@ size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int s
 // *why to a static message when the request itself is unsupported.
 cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why);
 
+// Block-scaled FP4 GEMM (kind::mxf4nvf4) on SM pairs; arguments validated by the caller.
+cudaError_t nvfp4_gemm_launch(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, void* D, int M,
+                              int N, int K, int out_f16, float alpha, cudaStream_t st, const char** why);
+
 // Device error word of the GEMM kernels (bounded-wait expiry).
 cudaError_t device_error_read(int* v);
 cudaError_t device_error_clear();

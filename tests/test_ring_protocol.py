@@ -3,44 +3,28 @@
 
 Each role replays, in order, the waits and arrivals the kernel issues: the raw-A
 producer (SPR raw stages per round of four k-blocks, at most `inflight` stages
-in flight), the B producer (one arrival with the round's bytes on rdy), the MMA
-issuer (one rdy wait and one fre commit per round; commits land later, like MMA
-completion), the epilogue and the sixteen decode warps (slice j decodes
-k-block j of every round and reads raw stage position j // RSK).  With a raw
-ring of at least two rounds a sync warp does the decode warps' mbarrier waits
-one round ahead and their arrivals, and hands rounds over through two pairs of
-named barriers; otherwise each decode warp waits and arrives itself.  TMA
-completions also land later.  An mbarrier wait is modelled the way the
-hardware answers a parity wait -- it passes when the barrier's current phase
-parity differs from the waited one -- and the model fails when that answer
-differs from the intended one (the phase completed or not), when an arrival
-lands in a phase other than the one it is meant for, when one generation of a
-named barrier collects arrivals meant for different rounds, or when no role
-can move.  The ring depths are the ones the launcher picks for each format and
-tile width, plus small rings."""
+in flight), the B producer (a ring of NBR round slots of its own: b_empty
+wait, one arrival with the round's bytes on b_full), the MMA issuer (b_full
+and rdy waits, one fre and one b_empty commit per round; commits land later,
+like MMA completion), the epilogue and the decode warps.  In group mode (a raw
+ring of at least NRND rounds) NG groups of eight decode warps take whole
+rounds in turn: each warp of group g waits for the round's TMEM slot (fre),
+then for its raw stages, and arrives on raw_empty and rdy.  In per-warp mode sixteen decode warps each
+decode one k-block of every round (slice j reads raw stage position j // RSK)
+and wait and arrive themselves.  TMA completions also land later.  An mbarrier
+wait is modelled the way the hardware answers a parity wait -- it passes when
+the barrier's current phase parity differs from the waited one -- and the
+model fails when that answer differs from the intended one (the phase
+completed or not), when an arrival lands in a phase other than the one it is
+meant for, or when no role can move.  The ring depths are the ones the
+launcher picks for each format and tile width, plus small rings."""
 import random
 
 import pytest
 
 SMEM_BUDGET = 224 * 1024
 DK = 4
-
-
-class NamedBar:
-    """A hardware named barrier: a generation completes after `count` arrivals;
-    bar.sync arrives and waits for the generation it arrived in."""
-
-    def __init__(self, name, count):
-        self.name, self.count, self.gen, self.tags = name, count, 0, []
-
-    def arrive(self, tag, who):
-        if self.tags:
-            assert self.tags[0] == tag, f"{who}: arrival for round {tag} in a generation of {self.name} for round {self.tags[0]}"
-        self.tags.append(tag)
-        gen = self.gen
-        if len(self.tags) == self.count:
-            self.tags, self.gen = [], self.gen + 1
-        return gen
+GW = 8  # decode warps per group
 
 
 class Bar:
@@ -54,21 +38,25 @@ class Bar:
             self.pending, self.c = 0, self.c + 1
 
 
-def run(units, RSK, SR, NRND, seed, syncw=None, inflight=2):
+def run(units, RSK, SR, NRND, seed, mode=None, ng=None, inflight=2, raw_first=False, nbr=2):
     """units: k-blocks per work unit of this CTA, in order; inflight: raw
     stages the producer keeps in flight (fewer than SR, as in TmemCfg: the
-    stage it waits for must not have been refilled; 0 = no bound)."""
+    stage it waits for must not have been refilled; 0 = no bound).  mode:
+    "groups" or "warps" (default: as TmemCfg picks); ng: decode groups in
+    group mode (default NRND); raw_first: a group waits for its raw stages
+    before its TMEM slot (the order the kernel does not use)."""
     SPR = DK // RSK
     inflight = min(inflight, SR - 1)
-    if syncw is None:
-        syncw = SR >= 2 * SPR
+    if mode is None:
+        mode = "groups" if SR // SPR >= NRND else "warps"
+    ng = NRND if ng is None else ng
     rng = random.Random(seed)
     raw_full = [Bar(f"raw_full{i}", 2) for i in range(SR)]  # producer arrive + TMA bytes
-    raw_empty = [Bar(f"raw_empty{i}", 1 if syncw else 4 * RSK) for i in range(SR)]
-    rdy = [Bar(f"rdy{i}", (1 if syncw else 16) + 2) for i in range(NRND)]  # decode side + B arrive + B bytes
-    start = [NamedBar(f"START{i}", 17) for i in range(2)]
-    done = [NamedBar(f"DONE{i}", 17) for i in range(2)]
+    raw_empty = [Bar(f"raw_empty{i}", GW if mode == "groups" else 4 * RSK) for i in range(SR)]
+    rdy = [Bar(f"rdy{i}", GW if mode == "groups" else 16) for i in range(NRND)]  # decode warps
     fre = [Bar(f"fre{i}", 1) for i in range(NRND)]
+    b_full = [Bar(f"b_full{i}", 2) for i in range(nbr)]  # B arrive + B bytes
+    b_empty = [Bar(f"b_empty{i}", 1) for i in range(nbr)]
     acc_full = [Bar(f"acc_full{i}", 1) for i in range(2)]
     acc_empty = [Bar(f"acc_empty{i}", 1) for i in range(2)]
     later = []
@@ -92,11 +80,11 @@ def run(units, RSK, SR, NRND, seed, syncw=None, inflight=2):
         r = 0
         for nr in rounds:
             for _ in range(nr):
-                slot, use = r % NRND, r // NRND
-                if use:
-                    yield ("wait", fre[slot], use - 1)
-                yield ("arrive", rdy[slot], use)
-                yield ("later", rdy[slot], use)
+                bs, buse = r % nbr, r // nbr
+                if buse:
+                    yield ("wait", b_empty[bs], buse - 1)
+                yield ("arrive", b_full[bs], buse)
+                yield ("later", b_full[bs], buse)
                 r += 1
 
     def mma():
@@ -107,8 +95,11 @@ def run(units, RSK, SR, NRND, seed, syncw=None, inflight=2):
                 yield ("wait", acc_empty[acc], k - 1)
             for _ in range(nr):
                 slot, use = r % NRND, r // NRND
+                bs, buse = r % nbr, r // nbr
+                yield ("wait", b_full[bs], buse)
                 yield ("wait", rdy[slot], use)
                 yield ("later", fre[slot], use)
+                yield ("later", b_empty[bs], buse)
                 r += 1
             yield ("later", acc_full[acc], k)
 
@@ -118,70 +109,53 @@ def run(units, RSK, SR, NRND, seed, syncw=None, inflight=2):
             yield ("wait", acc_full[acc], k)
             yield ("arrive", acc_empty[acc], k)
 
-    def decode(j):
+    def group_warp(g):
         r = 0
         for nr in rounds:
             for _ in range(nr):
-                if syncw:
-                    yield ("nsync", start[r & 1], r)
-                    yield ("narrive", done[r & 1], r)
-                else:
-                    st = r * SPR + j // RSK
-                    rs, fill = st % SR, st // SR
+                if r % ng == g:
                     slot, use = r % NRND, r // NRND
-                    yield ("wait", raw_full[rs], fill)
-                    if use:
-                        yield ("wait", fre[slot], use - 1)
-                    yield ("arrive", raw_empty[rs], fill)
+                    stages = [r * SPR + pos for pos in range(SPR)]
+                    raw_waits = [("wait", raw_full[st % SR], st // SR) for st in stages]
+                    slot_wait = [("wait", fre[slot], use - 1)] if use else []
+                    for op in (raw_waits + slot_wait if raw_first else slot_wait + raw_waits):
+                        yield op
+                    for st in stages:
+                        yield ("arrive", raw_empty[st % SR], st // SR)
                     yield ("arrive", rdy[slot], use)
                 r += 1
 
-    def sync_warp():
-        nr = sum(rounds)
-
-        def ready(r):
-            for pos in range(SPR):
-                st = r * SPR + pos
-                yield ("wait", raw_full[st % SR], st // SR)
-            if r // NRND:
-                yield ("wait", fre[r % NRND], r // NRND - 1)
-
-        if nr:
-            yield from ready(0)
-            yield ("narrive", start[0], 0)
-        for r in range(nr):
-            if r + 1 < nr:
-                yield from ready(r + 1)
-                yield ("narrive", start[(r + 1) & 1], r + 1)
-            yield ("nsync", done[r & 1], r)
-            for pos in range(SPR):
-                st = r * SPR + pos
-                yield ("arrive", raw_empty[st % SR], st // SR)
-            yield ("arrive", rdy[r % NRND], r // NRND)
+    def slice_warp(j):
+        r = 0
+        for nr in rounds:
+            for _ in range(nr):
+                st = r * SPR + j // RSK
+                rs, fill = st % SR, st // SR
+                slot, use = r % NRND, r // NRND
+                yield ("wait", raw_full[rs], fill)
+                if use:
+                    yield ("wait", fre[slot], use - 1)
+                yield ("arrive", raw_empty[rs], fill)
+                yield ("arrive", rdy[slot], use)
+                r += 1
 
     roles = {"raw producer": raw_producer(), "B producer": b_producer(), "MMA": mma(), "epilogue": epilogue()}
-    if syncw:
-        roles["sync warp"] = sync_warp()
     for q in range(4):
-        for j in range(4):
-            roles[f"decode q{q} s{j}"] = decode(j)
+        if mode == "groups":
+            for g in range(ng):
+                for h in range(GW // 4):
+                    roles[f"decode q{q} h{h} g{g}"] = group_warp(g)
+        else:
+            for j in range(4):
+                roles[f"decode q{q} s{j}"] = slice_warp(j)
     cur = {n: next(g, None) for n, g in roles.items()}
-    parked = {}  # role -> (named barrier, generation it waits for)
     while True:
         live = [n for n, op in cur.items() if op is not None]
         if not live and not later:
-            assert not any(b.tags for b in start + done), "named barrier left with arrivals"
             return
         ready = []
         for n in live:
             op = cur[n]
-            if n in parked:
-                nb, g = parked[n]
-                if nb.gen > g:
-                    del parked[n]
-                    cur[n] = next(roles[n], None)
-                    ready.append(None)  # progress was made
-                continue
             if op[0] == "wait":
                 bar, k = op[1], op[2]
                 hw = (bar.c & 1) != (k & 1)
@@ -190,13 +164,8 @@ def run(units, RSK, SR, NRND, seed, syncw=None, inflight=2):
                     ready.append(n)
             else:
                 ready.append(n)
-        if None in ready:
-            continue
         choices = ready + (["completion"] if later else [])
         assert choices, "no role can move: " + ", ".join(f"{n} waits {cur[n][1].name}" for n in live)
-        choices = [c for c in choices if c not in parked]
-        if not choices:
-            continue
         pick = rng.choice(choices)
         if pick == "completion":
             bar, k, who = later.pop(rng.randrange(len(later)))
@@ -207,11 +176,6 @@ def run(units, RSK, SR, NRND, seed, syncw=None, inflight=2):
             op[1].arrive(op[2], pick)
         elif op[0] == "later":
             later.append((op[1], op[2], pick))
-        elif op[0] == "narrive":
-            op[1].arrive(op[2], pick)
-        elif op[0] == "nsync":
-            parked[pick] = (op[1], op[1].arrive(op[2], pick))
-            continue
         cur[pick] = next(roles[pick], None)
 
 
@@ -219,17 +183,22 @@ ROW_BYTES = {"E2M1": 32, "E4M3": 64, "BF16": 128, "TF32": 256}
 
 
 def launcher_rings(fmt, bn):
-    """RSK, SR, NRND and stages in flight as the launcher (PickTmem) and
-    TmemCfg choose them."""
+    """RSK, SR, NRND, stages in flight and B ring slots as the launcher
+    (PickTmem) and TmemCfg choose them."""
     row = ROW_BYTES[fmt]
     rsk = 4 if row <= 64 else 2 if row == 128 else 1
     spr = DK // rsk
     nrnd = 3 if bn <= 32 else 2
     stage = rsk * row * 128
-    sr = min(12, (SMEM_BUDGET - 1024 - nrnd * 4 * bn * 128) // stage)
+    bround = DK * bn * 128
+    avail = SMEM_BUDGET - 1024
+    nbr_t = max(2, min(8, 65536 // bround))
+    nbr_g = (avail - nrnd * spr * stage) // bround
+    nbr = nbr_g if 2 <= nbr_g < nbr_t else nbr_t
+    sr = min(12, (avail - nbr * bround) // stage)
     sr = sr // spr * spr
-    inflight = max(1, 96 * 1024 // stage)
-    return rsk, sr, nrnd, inflight
+    inflight = sr - 1
+    return rsk, sr, nrnd, inflight, nbr
 
 
 UNITS = [[64], [20, 28, 64, 12], [13, 9], [66, 10], [1, 2, 3, 5]]
@@ -238,10 +207,10 @@ UNITS = [[64], [20, 28, 64, 12], [13, 9], [66, 10], [1, 2, 3, 5]]
 @pytest.mark.parametrize("fmt", list(ROW_BYTES))
 @pytest.mark.parametrize("bn", [16, 32, 64])
 def test_launcher_rings(fmt, bn):
-    rsk, sr, nrnd, inflight = launcher_rings(fmt, bn)
+    rsk, sr, nrnd, inflight, nbr = launcher_rings(fmt, bn)
     assert sr >= DK // rsk and sr % (DK // rsk) == 0
     for i, units in enumerate(UNITS):
-        run(units, rsk, sr, nrnd, seed=i, inflight=inflight)
+        run(units, rsk, sr, nrnd, seed=i, inflight=inflight, nbr=nbr)
 
 
 @pytest.mark.parametrize("rsk,sr,nrnd", [(4, 1, 2), (4, 2, 3), (2, 2, 2), (2, 4, 3), (1, 4, 2), (1, 8, 3)])
@@ -254,17 +223,44 @@ def test_small_rings(rsk, sr, nrnd):
 @pytest.mark.parametrize("rsk,sr,nrnd", [(4, 2, 2), (4, 3, 3), (2, 4, 2), (1, 8, 3)])
 def test_per_warp_protocol_on_deep_rings(rsk, sr, nrnd):
     """The per-warp protocol (used for TF32) is also sound on rings deep
-    enough for the sync warp."""
+    enough for the groups."""
     for i, units in enumerate(UNITS):
-        run(units, rsk, sr, nrnd, seed=20 + i, syncw=False)
+        run(units, rsk, sr, nrnd, seed=20 + i, mode="warps")
 
 
-def test_model_flags_sync_warp_on_one_round_ring():
-    """The sync warp waits for round r + 1's raw stages before it releases
-    round r's: with a ring of a single round that is a deadlock, which is why
-    such rings use the per-warp protocol."""
-    with pytest.raises(AssertionError, match="no role can move"):
-        run([64], 4, 1, 3, seed=0, syncw=True, inflight=0)
+def _fails(**kw):
+    failures = 0
+    for seed in range(40):
+        for units in UNITS:
+            try:
+                run(units, seed=seed, **kw)
+            except AssertionError:
+                failures += 1
+    return failures
+
+
+def test_model_flags_more_groups_than_round_slots():
+    """With more decode groups than TMEM round slots a group can reach round
+    r while the MMAs of round r - 2 NRND have not run: its parity wait on the
+    slot passes on a stale phase.  The kernel uses NG = NRND."""
+    assert _fails(RSK=4, SR=6, NRND=2, mode="groups", ng=3, inflight=0) > 0
+
+
+def test_model_flags_raw_ring_shorter_than_round_slots():
+    """With a raw ring of fewer than NRND rounds the slot wait no longer
+    implies that the previous fill of each raw stage has landed: the raw wait
+    can pass on a stale phase.  The kernel uses group mode only when the ring
+    holds NRND rounds."""
+    assert _fails(RSK=4, SR=2, NRND=3, mode="groups", inflight=0) > 0
+
+
+def test_model_flags_raw_wait_before_slot_wait():
+    """Waiting for the raw stages before the round's TMEM slot loses the
+    guarantee when the ring depth is not a multiple of the group count (the
+    group did not itself wait on the slot's previous fill): it can see a raw
+    slot two fills behind.  Slot first, the same ring is sound."""
+    assert _fails(RSK=4, SR=4, NRND=3, mode="groups", inflight=0, raw_first=True) > 0
+    assert _fails(RSK=4, SR=4, NRND=3, mode="groups", inflight=0) == 0
 
 
 def test_model_flags_inflight_bound_beyond_ring():
