@@ -891,6 +891,20 @@ def profile_case(case: str):
         print(json.dumps({"profile_case": case, "ok": True}))
         return
     M, N, K = (int(v) for v in shape.lower().split("x"))
+    if fname == "nvfp4gemm":  # the block-scaled FP4 GEMM (kind::mxf4nvf4)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(94)
+        A = torch.randint(0, 256, (M, K // 2), generator=g, device="cuda", dtype=torch.uint8)
+        B = torch.randint(0, 256, (N, K // 2), generator=g, device="cuda", dtype=torch.uint8)
+        SA = torch.randint(0x30, 0x48, (M, K // 16), generator=g, device="cuda", dtype=torch.uint8)
+        SB = torch.randint(0x30, 0x48, (N, K // 16), generator=g, device="cuda", dtype=torch.uint8)
+        D = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        for _ in range(5):
+            tb.gemm_nvfp4(A, SA, B, SB, D, M, N, K, out=tb.Out.F16, alpha=1e-4)
+        torch.cuda.synchronize()
+        assert tb.device_error() == 0, "a kernel reported a device-side wait timeout"
+        print(json.dumps({"profile_case": case, "ok": True}))
+        return
     if fname == "e4m3xe4m3":  # the native FP8 GEMM (both operands E4M3, per-tensor scales)
         A, sa = weights_q(torch, tb, tb.Format.E4M3, M, K, 0.02, seed=1)
         B, sb = weights_q(torch, tb, tb.Format.E4M3, N, K, 1.0, seed=2)
@@ -939,7 +953,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the MLP-shape and 8192^3 FP4 sub-objects")
     ap.add_argument("--profile-case", metavar="FMT:MxNxK",
                     help="run only 5 fused weight-only GEMMs of this case (e.g. e4m3:14336x16x4096; f16:MxNxK for "
-                         "the plain FP16 GEMM, e4m3xe4m3:MxNxK for the native FP8 GEMM, nvfp4:ROWSxCOLS for 5 "
+                         "the plain FP16 GEMM, e4m3xe4m3:MxNxK for the native FP8 GEMM, nvfp4gemm:MxNxK for the "
+                         "block-scaled FP4 GEMM, nvfp4:ROWSxCOLS for 5 "
                          "block-scaled FP4 decodes) and exit; "
                          "the command profiles/ captures of single kernels use")
     args = ap.parse_args()

@@ -18,8 +18,13 @@
 // tile.  With every stage the producer also brings in those scale bytes (two
 // TMA boxes, 16 bytes x 128 and 16 bytes x 256 rows) on a barrier of its own
 // CTA; four SF warps then copy them from shared to tensor memory with
-// tcgen05.st into the stage's scale slot and arrive on the leader's sf_full
-// barrier.  A stage and its scale slot are refilled only after the pair's
+// tcgen05.st into the stage's scale slot and signal the leader's sf_full
+// barrier: the leader's SF warps arrive locally (one of them arming the
+// barrier for the other CTA's bytes), the other CTA's SF warps each send a
+// 16-byte DSMEM bulk copy whose completion counts on it.  A cluster-scope
+// release arrival per warp and k-block (the first version) stalled the SF
+// warps on the memory barrier it implies (ncu: membar 7 per issue, tensor
+// pipe 24% active at 4096^3).  A stage and its scale slot are refilled only after the pair's
 // MMAs of their previous use have completed (the empty barrier the producer
 // waits on), so the SF warps need no wait of their own for the slot.
 //
@@ -66,7 +71,8 @@ struct Nvfp4Cfg {
     static constexpr int SF_BYTES = SFA_BYTES + SFB_BYTES;
     static constexpr int OFF_BAR = S * STAGE_BYTES;
     static constexpr int NUM_BARS = 4 * S + 3;
-    static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16;
+    static constexpr int OFF_SIG = OFF_BAR + ((NUM_BARS * 8 + 16 + 127) / 128) * 128;  // 4 x 16 B signal sources / sinks
+    static constexpr int SMEM_BYTES = OFF_SIG + 64;
     static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
     static constexpr int SF_WARP0 = 6;
     static constexpr int NUM_THREADS = (SF_WARP0 + 4) * 32;
@@ -149,7 +155,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&sf_full[s], 8);
+            mbar_init(&sf_full[s], 4);
             mbar_init(&empty[s], 1);
             mbar_init(&sf_land[s], 1);
         }
@@ -220,7 +226,7 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                 tc_fence_after();
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph, abort_flag))) { ok = false; break; }
-                    if (!__all_sync(0xFFFFFFFFu, mbar_wait_cluster(&sf_full[s], ph, abort_flag))) { ok = false; break; }
+                    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&sf_full[s], ph, abort_flag))) { ok = false; break; }
                     tc_fence_after();
                     if (elect_one()) {
                         const uint32_t a_lo = sdesc_lo(sbase + s * C::STAGE_BYTES);
@@ -299,7 +305,15 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(&sf_full[s], 0u);
+                if (lane == 0) {
+                    if (leader) {
+                        if (q == 0) mbar_arrive_expect_tx(&sf_full[s], 4u * 16u);  // the other CTA's four signals
+                        else mbar_arrive(&sf_full[s]);
+                    } else {
+                        uint8_t* sig = smem + C::OFF_SIG + q * 16;
+                        bulk_copy_to_cluster(cluster_addr(sig, 0u), sig, 16u, leader_bar(&sf_full[s]));
+                    }
+                }
                 if (++s == C::S) { s = 0; ph ^= 1u; }
             }
         }
