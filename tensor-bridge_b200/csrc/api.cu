@@ -226,7 +226,8 @@ size_t tb_gemm_fused_workspace(tb_format a_fmt, int M, int N, int K) {
 }
 
 static tb_status fused_request(tb_format a_fmt, const void* A, const uint16_t* B, void* D, long long ldd, int M, int N,
-                               int K, tb_out_type out, float alpha, void* ws, size_t ws_bytes, tb_stream_t stream) {
+                               int K, tb_out_type out, float alpha, void* ws, size_t ws_bytes, tb_stream_t stream,
+                               int max_ctas = 0) {
     if (a_fmt != TB_FMT_E4M3 && a_fmt != TB_FMT_E5M2 && a_fmt != TB_FMT_E2M1 && a_fmt != TB_FMT_E2M1_UNPACKED &&
         a_fmt != TB_FMT_BF16 && a_fmt != TB_FMT_TF32 && a_fmt != TB_FMT_F16)
         return fail(TB_ERR_INVALID_ARGUMENT, "format %d is not a fused weight format", (int)a_fmt);
@@ -246,6 +247,7 @@ static tb_status fused_request(tb_format a_fmt, const void* A, const uint16_t* B
     r.alpha = alpha;
     r.workspace = ws;
     r.workspace_bytes = ws_bytes;
+    r.max_ctas = max_ctas;
     return launch_gemm(r, stream);
 }
 
@@ -396,3 +398,8 @@ tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, i
 }
 
 }  // extern "C"
+
+tb_status tb::gemm_fused_capped(tb_format a_fmt, const void* A, const uint16_t* B, void* D, int M, int N, int K,
+                                tb_out_type out, float alpha, int max_ctas, tb_stream_t stream) {
+    return fused_request(a_fmt, A, B, D, N, M, N, K, out, alpha, nullptr, 0, stream, max_ctas);
+}

@@ -188,6 +188,8 @@ struct GemmArgs {
     // BN / 2-column halves of the tiles from half_from on (a partial last wave
     // split along N; == num_units when there are none).
     int half_from;
+    // Host side only: at most this many CTAs (SMs) for the launch (0: all).
+    int grid_cap;
 };
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) ----------------------

@@ -1,6 +1,13 @@
 // sharded.cu -- column-sharded (output-feature-sharded) weight GEMM with an
 // NCCL all-gather of the output row blocks, overlapped block by block.
 //
+// Overlap needs SMs for both at once: the fused GEMM is persistent and its
+// CTAs take about 225 KB of shared memory, so an all-gather kernel cannot
+// share an SM with it.  The communicator is therefore created with at most
+// kCommCtas CTAs per collective (ncclCommInitRankConfig, maxCTAs) and the
+// sharded GEMM runs on the other SMs; the all-gather of block group c then
+// proceeds beside the GEMM of block c + 1 instead of after it.
+//
 // NCCL is resolved at run time (dlopen of libnccl.so.2, reusing a copy that
 // is already loaded in the process), so the library itself does not link
 // NCCL and loads on machines without it.
@@ -20,6 +27,7 @@ namespace {
 struct NcclApi {
     ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
     ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     ncclResult_t (*comm_count)(const ncclComm_t, int*) = nullptr;
     ncclResult_t (*comm_user_rank)(const ncclComm_t, int*) = nullptr;
@@ -39,6 +47,8 @@ const NcclApi& nccl() {
         auto sym = [h](const char* n) { return dlsym(h, n); };
         api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
         api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+        api.comm_init_rank_config =
+            reinterpret_cast<decltype(api.comm_init_rank_config)>(sym("ncclCommInitRankConfig"));
         api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
         api.comm_count = reinterpret_cast<decltype(api.comm_count)>(sym("ncclCommCount"));
         api.comm_user_rank = reinterpret_cast<decltype(api.comm_user_rank)>(sym("ncclCommUserRank"));
@@ -49,6 +59,10 @@ const NcclApi& nccl() {
     });
     return api;
 }
+
+// CTAs an NCCL collective of this library's communicators may use, and so the
+// SMs the sharded GEMM leaves free for it.
+constexpr int kCommCtas = 16;
 
 tb_status nccl_fail(ncclResult_t r, const char* what) {
     const NcclApi& n = nccl();
@@ -79,7 +93,14 @@ tb_status tb_nccl_comm_init(void** comm_out, int world, int rank, const uint8_t 
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof uid);
     ncclComm_t c = nullptr;
-    ncclResult_t r = n.comm_init_rank(&c, world, uid, rank);
+    ncclResult_t r;
+    if (n.comm_init_rank_config) {
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.maxCTAs = kCommCtas;
+        r = n.comm_init_rank_config(&c, world, uid, rank, &cfg);
+    } else {
+        r = n.comm_init_rank(&c, world, uid, rank);
+    }
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
     *comm_out = c;
     return TB_OK;
@@ -109,6 +130,9 @@ tb_status tb_gemm_sharded_fused(tb_format a_fmt, const void* A_shard, const uint
     const size_t elem = out == TB_OUT_F16 ? 2 : 4;
     const size_t block_elems = static_cast<size_t>(Mc) * N;
     const size_t a_block_bytes = tb::stored_bytes(a_fmt, static_cast<size_t>(Mc) * K);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return TB_ERR_CUDA;
+    const int sms = tb::device_info(dev).sms;
 
     cudaEvent_t done[64];
     if (chunks > 64) return TB_ERR_INVALID_ARGUMENT;
@@ -123,7 +147,7 @@ tb_status tb_gemm_sharded_fused(tb_format a_fmt, const void* A_shard, const uint
         const size_t g0 = static_cast<size_t>(c * world + rank) * Mc;  // global first row of this block
         char* dblk = static_cast<char*>(D) + g0 * N * elem;
         const void* ablk = static_cast<const char*>(A_shard) + c * a_block_bytes;
-        st = tb_gemm_fused(a_fmt, ablk, B, dblk, Mc, N, K, out, alpha, nullptr, 0, stream);
+        st = tb::gemm_fused_capped(a_fmt, ablk, B, dblk, Mc, N, K, out, alpha, sms - kCommCtas, stream);
         if (st != TB_OK) break;
         if (cudaEventRecord(done[c], stream) != cudaSuccess || cudaStreamWaitEvent(comm_stream, done[c], 0) != cudaSuccess) {
             st = TB_ERR_CUDA;

@@ -42,6 +42,7 @@ struct GemmRequest {
     size_t workspace_bytes;
     int force_bn;       // 0 = choose automatically (for tests and tuning)
     int force_splits;   // 0 = choose automatically
+    int max_ctas;       // > 0: use at most this many SMs (leaves the rest to a concurrent kernel)
 };
 
 // Split-K workspace needed by a fused/f16 GEMM of this shape (0 if none).
@@ -50,6 +51,11 @@ size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int s
 // Validated launch.  Returns cudaSuccess or the failing CUDA error; sets
 // *why to a static message when the request itself is unsupported.
 cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why);
+
+// api.cu: tb_gemm_fused on at most max_ctas SMs (the sharded GEMM leaves the
+// other SMs to the concurrent NCCL all-gather).
+tb_status gemm_fused_capped(tb_format a_fmt, const void* A, const uint16_t* B, void* D, int M, int N, int K,
+                            tb_out_type out, float alpha, int max_ctas, tb_stream_t stream);
 
 // Block-scaled FP4 GEMM (kind::mxf4nvf4) on SM pairs; arguments validated by the caller.
 cudaError_t nvfp4_gemm_launch(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, void* D, int M,
