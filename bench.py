@@ -14,8 +14,10 @@ native kind::f8f6f4 tensor-core path; FP32 output, as the reference.  That is
 The same JSON line also carries, measured after the timed steps, the
 weight-only MLP shapes (W 14336x4096 and 4096x14336, 1-2048 tokens, GB/s
 against HBM), the 8192^3 fused FP4 GEMM with FP16 output, and the
-16384x53248 E4M3 weight GEMM column-sharded over the N GPUs with an NCCL
-all-gather of the output (strong scaling).
+16384x53248 E4M3 weight GEMM column-sharded over the N GPUs, every rank ending
+with the whole output: the fused kernel's epilogue stores each tile into the
+peers' D over NVLink, with the NCCL all-gather variant timed beside it
+(strong scaling).
 
 On N GPUs (torchrun) every rank runs the same sweep on its own data (the
 sweep has no exchange step): weak scaling, value = all ranks' flops / the
@@ -639,22 +641,33 @@ def config_256(torch, tb, iters: int = 50):
 def sharded_weight_gemm(torch, tb, dist, steps: int = 5, warmup: int = 2):
     """The 16384 x 53248 E4M3 weight (N(0, 0.02), per-tensor scale 448/maxabs),
     used as its transpose in the weight role: M = 53248 output rows, K = 16384;
-    X = 8192 FP16 tokens from N(0, 1), replicated; FP16 output.  On N GPUs the
-    output rows are split block-cyclically (4 chunks per rank), each rank runs
-    the fused kernel on its rows and NCCL all-gathers D in place, overlapped
-    chunk by chunk; on one GPU it is one fused GEMM.  Device time, max over ranks."""
+    X = 8192 FP16 tokens from N(0, 1), replicated; FP16 output.  On one GPU it
+    is one fused GEMM.  On N GPUs the output rows are split over the ranks and
+    every rank ends with all of D, two ways:
+      p2p   (the product path) each rank's fused kernel stores every finished
+            tile into all ranks' D over NVLink (peer-mapped buffers), one
+            launch over the rank's M / N contiguous rows;
+      nccl  block-cyclic rows in 4 chunks per rank, the fused kernel per
+            chunk, NCCL all-gathers in place on a second stream.
+    Each is checked after timing.  Also timed: the rank's GEMM alone (all SMs,
+    no exchange) and the NCCL all-gathers alone.  Device time, max over ranks."""
     M, N, K = 53248, 8192, 16384
     world, rank = dist.world, dist.rank
-    chunks = 4 if world > 1 else 1
+    chunks = 4
     g = torch.Generator(device="cuda")
     g.manual_seed(5)
     W = torch.randn(M, K, generator=g, device="cuda") * 0.02
     amax = torch.zeros(1, dtype=torch.float32, device="cuda")
     tb.absmax(W, W.numel(), amax)
     scale = float(np.float32(448.0) / np.float32(float(amax.item())))
-    rows = W if world == 1 else tb.shard_rows(W, M, world, chunks, rank)
-    A = torch.empty(rows.numel(), dtype=torch.uint8, device="cuda")
-    tb.quantize(tb.Format.E4M3, rows, A, rows.numel(), scale=scale)
+
+    def quantized(rows):
+        q = torch.empty(rows.numel(), dtype=torch.uint8, device="cuda")
+        tb.quantize(tb.Format.E4M3, rows, q, rows.numel(), scale=scale)
+        return q
+
+    A1 = quantized(W if world == 1 else tb.shard_rows(W, M, world, 1, rank))  # contiguous rows
+    A4 = quantized(tb.shard_rows(W, M, world, chunks, rank)) if world > 1 else None
     # Rows kept for the check after timing: 8 from each of the world*chunks
     # row blocks (a block straddles 128-row tile boundaries at offsets that
     # differ per block), computed by every rank or gathered from the others.
@@ -663,84 +676,87 @@ def sharded_weight_gemm(torch, tb, dist, steps: int = 5, warmup: int = 2):
     sample = torch.tensor(sorted({b * mc + (37 * b + 120 + 3 * i) % mc for b in range(nblk) for i in range(8)}),
                           device="cuda")
     W_s = W[sample].contiguous()
-    del W, rows
+    del W
     g.manual_seed(6)
     X = torch.randn(N, K, generator=g, device="cuda").half()
     D = torch.empty(M, N, dtype=torch.float16, device="cuda")
     alpha = float(np.float32(1.0) / np.float32(scale))
-    comm = None
     st, cst = torch.cuda.Stream(), torch.cuda.Stream()
-    if world > 1:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return dist.max(e0.elapsed_time(e1) / steps)
+
+    flops = 2.0 * M * N * K
+    res = {"M": M, "N": N, "K": K, "fmt": "e4m3", "out": "f16", "world": world, "scaling": "strong",
+           "allgather_bytes_per_rank": (world - 1) * (M // world) * N * 2 if world > 1 else 0}
+    if world == 1:
+        ms = timed(lambda: tb.gemm_fused(tb.Format.E4M3, A1, X, D, M, N, K, out=tb.Out.F16, alpha=alpha,
+                                         stream=st.cuda_stream))
+        check = sharded_check(torch, tb, dist, W_s, sample, X, D, N, K, scale, alpha)
+        res.update({"path": "one fused GEMM", "ms": ms, "gemm_only_ms": ms, "check": check})
+    else:
         uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
         if rank == 0:
             uid.copy_(torch.frombuffer(bytearray(tb.nccl_unique_id()), dtype=torch.uint8))
         dist.dist.broadcast(uid, 0)
         comm = tb.nccl_comm_init(world, rank, bytes(uid.cpu().numpy()))
+        try:
+            # p2p: one launch per rank over its contiguous M / world rows
+            handle = tb.peer_buffer_register(comm, D, stream=st.cuda_stream)
+            try:
+                p2p_ms = timed(lambda: tb.gemm_sharded_fused_p2p(tb.Format.E4M3, A1, X, handle, M, N, K, chunks=1,
+                                                                 out=tb.Out.F16, alpha=alpha, stream=st.cuda_stream))
+                D.fill_(float("nan"))  # the check must see D written by the p2p path alone
+                torch.cuda.synchronize()
+                tb.gemm_sharded_fused_p2p(tb.Format.E4M3, A1, X, handle, M, N, K, chunks=1, out=tb.Out.F16,
+                                          alpha=alpha, stream=st.cuda_stream)
+                torch.cuda.synchronize()
+                p2p_check = sharded_check(torch, tb, dist, W_s, sample, X, D, N, K, scale, alpha)
+            finally:
+                tb.peer_buffer_release(handle, stream=st.cuda_stream)
+            ml = M // world
+            gemm_ms = timed(lambda: tb.gemm_fused(tb.Format.E4M3, A1, X, D[rank * ml:(rank + 1) * ml], ml, N, K,
+                                                  out=tb.Out.F16, alpha=alpha, stream=st.cuda_stream))
 
-    def step():
-        if comm is None:
-            tb.gemm_fused(tb.Format.E4M3, A, X, D, M, N, K, out=tb.Out.F16, alpha=alpha, stream=st.cuda_stream)
-        else:
-            tb.gemm_sharded_fused(tb.Format.E4M3, A, X, D, M, N, K, comm, chunks, out=tb.Out.F16, alpha=alpha,
-                                  stream=st.cuda_stream, comm_stream=cst.cuda_stream)
+            # nccl: block-cyclic chunks, in-place all-gathers on a second stream
+            def nccl_step():
+                tb.gemm_sharded_fused(tb.Format.E4M3, A4, X, D, M, N, K, comm, chunks, out=tb.Out.F16,
+                                      alpha=alpha, stream=st.cuda_stream, comm_stream=cst.cuda_stream)
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(steps):
-        step()
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms = dist.max(e0.elapsed_time(e1) / steps)
-    dist.barrier()
-    # The two parts alone: this rank's block GEMMs on all SMs (no all-gather),
-    # and the all-gathers alone (through torch's NCCL group, same volume).
-    gemm_ms, ag_ms = ms, 0.0
-    if comm is not None:
-        mc = M // (world * chunks)
-        blk = A.numel() // chunks
+            nccl_ms = timed(nccl_step)
+            mcw = M // (world * chunks)
 
-        def gemm_only():
-            for c in range(chunks):
-                tb.gemm_fused(tb.Format.E4M3, A[c * blk:(c + 1) * blk], X, D[c * mc:(c + 1) * mc], mc, N, K,
-                              out=tb.Out.F16, alpha=alpha, stream=st.cuda_stream)
+            def ag_only():
+                with torch.cuda.stream(st):
+                    for c in range(chunks):
+                        grp = D[c * world * mcw:(c + 1) * world * mcw]
+                        dist.dist.all_gather_into_tensor(grp, grp[rank * mcw:(rank + 1) * mcw])
 
-        def ag_only():
-            with torch.cuda.stream(st):
-                for c in range(chunks):
-                    grp = D[c * world * mc:(c + 1) * world * mc]
-                    dist.dist.all_gather_into_tensor(grp, grp[rank * mc:(rank + 1) * mc])
-
-        for fn in (gemm_only, ag_only):
-            fn()
+            ag_ms = timed(ag_only)
+            D.fill_(float("nan"))
             torch.cuda.synchronize()
-            dist.barrier()
-            e0.record(st)
-            for _ in range(steps):
-                fn()
-            e1.record(st)
+            nccl_step()
             torch.cuda.synchronize()
-            v = dist.max(e0.elapsed_time(e1) / steps)
-            if fn is gemm_only:
-                gemm_ms = v
-            else:
-                ag_ms = v
-        # restore D (the parts above overwrote blocks of it) for the check
-        step()
-        torch.cuda.synchronize()
-        dist.barrier()
-    if comm is not None:
-        tb.nccl_comm_destroy(comm)
-    check = sharded_check(torch, tb, dist, W_s, sample, X, D, N, K, scale, alpha)
-    flops = 2.0 * M * N * K
-    return {"M": M, "N": N, "K": K, "fmt": "e4m3", "out": "f16", "world": world, "chunks": chunks,
-            "scaling": "strong", "ms": ms, "tflops_total": flops / ms / 1e9,
-            "tflops_per_gpu": flops / ms / 1e9 / world,
-            "allgather_bytes_per_rank": (world - 1) * (M // world) * N * 2 if world > 1 else 0,
-            "gemm_only_ms": gemm_ms, "allgather_only_ms": ag_ms, "check": check}
+            nccl_check = sharded_check(torch, tb, dist, W_s, sample, X, D, N, K, scale, alpha)
+        finally:
+            torch.cuda.synchronize()
+            tb.nccl_comm_destroy(comm)
+        res.update({"path": "p2p: fused GEMM epilogue stores tiles into peers' D", "ms": p2p_ms,
+                    "gemm_only_ms": gemm_ms, "check": p2p_check,
+                    "nccl": {"chunks": chunks, "ms": nccl_ms, "allgather_only_ms": ag_ms, "check": nccl_check}})
+    res["tflops_total"] = flops / res["ms"] / 1e9
+    res["tflops_per_gpu"] = res["tflops_total"] / world
+    return res
 
 
 def sharded_check(torch, tb, dist, W_s, sample, X, D, N: int, K: int, scale: float, alpha: float):
@@ -1133,8 +1149,10 @@ def targets(line: dict) -> dict:
     t["int8_pct_i8_dense"] = r(line["int8_4096"]["pct_i8_dense_peak"])
     sh = line["sharded_weight_gemm"]
     t["sharded"] = {"world": sh["world"], "ms": r(sh["ms"], 3), "gemm_only_ms": r(sh.get("gemm_only_ms"), 3),
-                    "allgather_only_ms": r(sh.get("allgather_only_ms"), 3), "check_pass": sh["check"]["pass"],
-                    "rel_frob": float(f"{sh['check']['rel_frob_max_vs_fp64']:.2e}")}
+                    "check_pass": sh["check"]["pass"], "rel_frob": float(f"{sh['check']['rel_frob_max_vs_fp64']:.2e}")}
+    if "nccl" in sh:
+        t["sharded"]["nccl"] = {"ms": r(sh["nccl"]["ms"], 3), "allgather_only_ms": r(sh["nccl"]["allgather_only_ms"], 3),
+                                "check_pass": sh["nccl"]["check"]["pass"]}
     c1 = line["config_256_e4m3"]
     t["config_256"] = {"us": r(c1["us"], 2), "rel_frob_vs_fp32_pct": r(100 * c1["rel_frob_vs_unquantized_fp32"], 3)}
     nv = (line.get("cpu_baseline") or {}).get("naive_single_thread")

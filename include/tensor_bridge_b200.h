@@ -307,6 +307,33 @@ tb_status tb_gemm_sharded_fused(tb_format a_fmt, const void* A_shard, const uint
                                 int M, int N, int K, tb_out_type out, float alpha, void* comm,
                                 int chunks, tb_stream_t stream, tb_stream_t comm_stream);
 
+/* The same sharded GEMM without a collective kernel: the fused kernel's
+ * epilogue stores every finished output tile into each other rank's D through
+ * peer-mapped memory (plain stores over NVLink), while the next tile's MMAs
+ * run.  D is a buffer registered once with tb_peer_buffer_register; block
+ * layout, shapes and the result are those of tb_gemm_sharded_fused, and
+ * chunks = 1 is the natural choice (the overlap is per tile, not per block).
+ * One process per GPU; the fused pair kernel must support the format (every
+ * stored format except F16).  Collective: every rank calls it with the same
+ * arguments, in the same order as its other calls on `comm`.  On `stream`, a
+ * one-word NCCL all-reduce before the GEMM (no rank writes into a peer's D
+ * before that peer has reached this call) and one after it (on completion
+ * every rank's D is whole). */
+tb_status tb_gemm_sharded_fused_p2p(tb_format a_fmt, const void* A_shard, const uint16_t* B, void* peer_buffer,
+                                    int M, int N, int K, tb_out_type out, float alpha, int chunks,
+                                    tb_stream_t stream);
+
+/* Collective over `comm`: maps every rank's `bytes`-byte device buffer `buf`
+ * (a cudaMalloc allocation or part of one, 16-byte aligned, the same size on
+ * all ranks) into every other rank's process with CUDA IPC, and returns the
+ * handle for tb_gemm_sharded_fused_p2p.  Synchronises `stream`.  Fails on all
+ * ranks (TB_ERR_INVALID_ARGUMENT or TB_ERR_CUDA) if it fails on one. */
+tb_status tb_peer_buffer_register(void* comm, void* buf, size_t bytes, tb_stream_t stream, void** peer_buffer_out);
+/* Collective: waits (on `stream`, synchronised) until every rank has reached
+ * it, then unmaps the peers' buffers.  Call it on every rank before any rank
+ * frees its buffer. */
+tb_status tb_peer_buffer_release(void* peer_buffer, tb_stream_t stream);
+
 /* NCCL plumbing (NCCL is loaded at run time; TB_ERR_NCCL if absent). */
 tb_status tb_nccl_unique_id(uint8_t id_out[128]);
 tb_status tb_nccl_comm_init(void** comm_out, int world, int rank, const uint8_t id[128]);

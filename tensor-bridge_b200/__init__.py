@@ -108,6 +108,9 @@ SIGNATURES = {
     "tb_gemm_fp8_fused_int8": (_st, [_p, _p, _p, _i, _i, _i, _f, _p, _sz, _p]),
     "tb_gemm_fp8_fused_int8_workspace": (_sz, [_i, _i, _i]),
     "tb_gemm_sharded_fused": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _p, _i, _p, _p]),
+    "tb_gemm_sharded_fused_p2p": (_st, [_i, _p, _p, _p, _i, _i, _i, _i, _f, _i, _p]),
+    "tb_peer_buffer_register": (_st, [_p, _p, _sz, _p, ctypes.POINTER(_p)]),
+    "tb_peer_buffer_release": (_st, [_p, _p]),
     "tb_nccl_unique_id": (_st, [ctypes.c_char_p]),
     "tb_nccl_comm_init": (_st, [ctypes.POINTER(_p), _i, _i, ctypes.c_char_p]),
     "tb_nccl_comm_destroy": (_st, [_p]),
@@ -300,3 +303,28 @@ def gemm_sharded_fused(fmt, A_shard, B, D, M: int, N: int, K: int, comm: int, ch
     in-place NCCL all-gathers on comm_stream; every rank ends with all of D."""
     call("tb_gemm_sharded_fused", int(fmt), _ptr(A_shard), _ptr(B), _ptr(D), M, N, K, int(out), alpha, comm,
          chunks, _stream(stream), _ptr(comm_stream) if comm_stream is not None else _stream(None))
+
+
+def peer_buffer_register(comm: int, D, nbytes: int = None, stream=None) -> int:
+    """Collective: map every rank's device buffer D (a torch tensor or pointer;
+    same byte size on all ranks) into the other ranks' processes for
+    gemm_sharded_fused_p2p.  Returns the handle."""
+    h = ctypes.c_void_p()
+    if nbytes is None:
+        nbytes = D.numel() * D.element_size()
+    call("tb_peer_buffer_register", comm, _ptr(D), nbytes, _stream(stream), ctypes.byref(h))
+    return h.value
+
+
+def peer_buffer_release(handle: int, stream=None):
+    """Collective: unmap the peers' buffers once every rank has reached it."""
+    call("tb_peer_buffer_release", handle, _stream(stream))
+
+
+def gemm_sharded_fused_p2p(fmt, A_shard, B, peer_buffer: int, M: int, N: int, K: int, chunks: int = 1,
+                           out=Out.F32, alpha: float = 1.0, stream=None):
+    """The sharded GEMM of gemm_sharded_fused whose fused-kernel epilogue stores
+    every output tile into all ranks' registered D (peer_buffer) over NVLink;
+    no NCCL data kernel."""
+    call("tb_gemm_sharded_fused_p2p", int(fmt), _ptr(A_shard), _ptr(B), peer_buffer, M, N, K, int(out), alpha,
+         chunks, _stream(stream))

@@ -227,7 +227,7 @@ size_t tb_gemm_fused_workspace(tb_format a_fmt, int M, int N, int K) {
 
 static tb_status fused_request(tb_format a_fmt, const void* A, const uint16_t* B, void* D, long long ldd, int M, int N,
                                int K, tb_out_type out, float alpha, void* ws, size_t ws_bytes, tb_stream_t stream,
-                               int max_ctas = 0) {
+                               int n_peers = 0, void* const* peer_D = nullptr) {
     if (a_fmt != TB_FMT_E4M3 && a_fmt != TB_FMT_E5M2 && a_fmt != TB_FMT_E2M1 && a_fmt != TB_FMT_E2M1_UNPACKED &&
         a_fmt != TB_FMT_BF16 && a_fmt != TB_FMT_TF32 && a_fmt != TB_FMT_F16)
         return fail(TB_ERR_INVALID_ARGUMENT, "format %d is not a fused weight format", (int)a_fmt);
@@ -247,7 +247,8 @@ static tb_status fused_request(tb_format a_fmt, const void* A, const uint16_t* B
     r.alpha = alpha;
     r.workspace = ws;
     r.workspace_bytes = ws_bytes;
-    r.max_ctas = max_ctas;
+    r.n_peers = n_peers;
+    r.peer_D = peer_D;
     return launch_gemm(r, stream);
 }
 
@@ -399,7 +400,8 @@ tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, i
 
 }  // extern "C"
 
-tb_status tb::gemm_fused_capped(tb_format a_fmt, const void* A, const uint16_t* B, void* D, int M, int N, int K,
-                                tb_out_type out, float alpha, int max_ctas, tb_stream_t stream) {
-    return fused_request(a_fmt, A, B, D, N, M, N, K, out, alpha, nullptr, 0, stream, max_ctas);
+tb_status tb::gemm_fused_to_peers(tb_format a_fmt, const void* A, const uint16_t* B, void* D, int M, int N, int K,
+                                  tb_out_type out, float alpha, int n_peers, void* const* peer_D, tb_stream_t stream) {
+    if (a_fmt == TB_FMT_F16) return fail(TB_ERR_INVALID_ARGUMENT, "peer copies need a stored weight format, not F16");
+    return fused_request(a_fmt, A, B, D, N, M, N, K, out, alpha, nullptr, 0, stream, n_peers, peer_D);
 }

@@ -28,7 +28,9 @@
 //               overlaps the first half's MMAs
 //   warps 2-5   epilogue: this CTA's 128 rows from its own TMEM; after each
 //               half each warp arrives on the leader's accumulator-empty
-//               barrier of that half
+//               barrier of that half.  With peer buffers (the sharded GEMM)
+//               each warp then copies its 32 finished rows from D into every
+//               other GPU's D over NVLink, while the next tile's MMAs run
 //   warp 6      TMA producer of this CTA's raw A rows into the raw ring
 //   warps 7-    decode warps (as in the one-CTA fused kernel): for each
 //               k-block, read the raw slice, decode to FP16, write the
@@ -105,6 +107,72 @@ __device__ __forceinline__ void pair_tile(const GemmArgs& p, int u, int tiles_m,
     } else {
         tm = u % tiles_m;
         tn = u / tiles_m;
+    }
+}
+
+// Copies rows [row0, row0 + 32) of the pair tile at column col0 from D to the
+// same place in every peer buffer (GemmArgs::peer_D).  Consecutive lanes take
+// consecutive 16-byte chunks of a row, so a warp's loads and stores cover 512
+// contiguous bytes; each lane keeps PUSH_ITEMS chunks in flight.  The loads
+// hit L2 (the epilogue has just written the rows); the stores cross NVLink.
+// The rows were stored by this warp's lanes: the caller's __syncwarp orders
+// those stores before these loads.  Peer buffers have D's alignment (16 bytes
+// or more), so vec_ok holds for them too.
+template <int BN>
+__device__ __forceinline__ void push_rows_to_peers(const GemmArgs& p, int row0, int col0, int lane) {
+    const int nrows = min(32, p.M - row0);
+    const int ncols = min(BN, p.N - col0);
+    if (nrows <= 0 || ncols <= 0) return;
+    const size_t esz = p.out_f16 ? 2 : 4;
+    const size_t ld_bytes = static_cast<size_t>(p.ldd) * esz;
+    const size_t base = static_cast<size_t>(row0) * ld_bytes + static_cast<size_t>(col0) * esz;
+    const char* src = static_cast<const char*>(p.D);
+    const int n16 = p.vec_ok ? static_cast<int>((static_cast<size_t>(ncols) * esz) >> 4) : 0;
+    const int items = nrows * n16;
+    constexpr int PUSH_ITEMS = 4;  // (the epilogue warps share the decode warps' register budget)
+    for (int q0 = 0; q0 < items; q0 += 32 * PUSH_ITEMS) {
+        uint4 v[PUSH_ITEMS];
+        size_t off[PUSH_ITEMS];
+#pragma unroll
+        for (int j = 0; j < PUSH_ITEMS; ++j) {
+            const int q = q0 + j * 32 + lane;
+            if (q < items) {
+                const int r = q / n16;
+                off[j] = base + static_cast<size_t>(r) * ld_bytes + static_cast<size_t>(q - r * n16) * 16u;
+                v[j] = __ldcg(reinterpret_cast<const uint4*>(src + off[j]));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxPeers; ++i) {
+            if (i >= p.n_peers) break;
+            char* dst = static_cast<char*>(p.peer_D[i]);
+#pragma unroll
+            for (int j = 0; j < PUSH_ITEMS; ++j)
+                if (q0 + j * 32 + lane < items) *reinterpret_cast<uint4*>(dst + off[j]) = v[j];
+        }
+    }
+    // Columns past the 16-byte chunks (a ragged last tile, or no vector
+    // access at all), one element at a time.
+    const int c0 = static_cast<int>((static_cast<size_t>(n16) * 16u) / esz);
+    const int tc = ncols - c0;
+    for (int q = lane; tc > 0 && q < nrows * tc; q += 32) {
+        const int r = q / tc;
+        const size_t o = base + static_cast<size_t>(r) * ld_bytes + static_cast<size_t>(c0 + q - r * tc) * esz;
+        if (esz == 2) {
+            const unsigned short x = __ldcg(reinterpret_cast<const unsigned short*>(src + o));
+#pragma unroll
+            for (int i = 0; i < kMaxPeers; ++i) {
+                if (i >= p.n_peers) break;
+                *reinterpret_cast<unsigned short*>(static_cast<char*>(p.peer_D[i]) + o) = x;
+            }
+        } else {
+            const unsigned int x = __ldcg(reinterpret_cast<const unsigned int*>(src + o));
+#pragma unroll
+            for (int i = 0; i < kMaxPeers; ++i) {
+                if (i >= p.n_peers) break;
+                *reinterpret_cast<unsigned int*>(static_cast<char*>(p.peer_D[i]) + o) = x;
+            }
+        }
     }
 }
 
@@ -261,7 +329,13 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(&acc_empty[h], 0u);
             }
+            // Sharded output: copy the tile's rows to the other GPUs while the
+            // MMAs of the next tile, which no longer need this accumulator, run.
+            if (p.n_peers > 0) push_rows_to_peers<C::BN>(p, tm * C::BM + my_row0 + quarter * 32, tn * C::BN, lane);
         }
+        // The peers read their D after the host's closing barrier: make this
+        // warp's stores to them visible system-wide before the grid ends.
+        if (p.n_peers > 0) __threadfence_system();
     } else if (warp == 6) {
         // ---------------- TMA producer: this CTA's raw A rows ----------------
         int s = 0;

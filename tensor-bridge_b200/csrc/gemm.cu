@@ -173,7 +173,7 @@ static cudaError_t launch_cfg(const CUtensorMap& ta, const CUtensorMap& tbm, con
         if (e != cudaSuccess) return e;
         attr_done.fetch_or(bit);
     }
-    const int sms = args.grid_cap > 0 ? args.grid_cap : device_info(dev).sms;
+    const int sms = device_info(dev).sms;
     const int grid = std::min(args.num_units, sms);
     k_gemm<C><<<grid, C::NUM_THREADS, C::SMEM_ALLOC, st>>>(ta, tbm, args);
     return cudaGetLastError();
@@ -450,7 +450,7 @@ static cudaError_t run_tmem(const GemmRequest& r, const GemmArgs& args, cudaStre
     cudaLaunchAttribute attr{};
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr.val.programmaticStreamSerializationAllowed = 1;
-    cfg.gridDim = dim3(std::min(args.num_units, args.grid_cap > 0 ? args.grid_cap : device_info(dev).sms), 1, 1);
+    cfg.gridDim = dim3(std::min(args.num_units, device_info(dev).sms), 1, 1);
     cfg.blockDim = dim3(C::NUM_THREADS, 1, 1);
     cfg.dynamicSmemBytes = C::SMEM_ALLOC;
     cfg.stream = st;
@@ -533,7 +533,7 @@ cudaError_t nvfp4_gemm_launch(const void* A, const uint8_t* sfa, const void* B, 
 
 cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why) {
     const int dev = current_device();
-    const int sms = r.max_ctas > 0 ? std::min(r.max_ctas, device_info(dev).sms) : device_info(dev).sms;
+    const int sms = device_info(dev).sms;
     const int bn = r.force_bn ? r.force_bn : choose_bn(r.N);
     const int tiles_m = (r.M + 127) / 128;
     const int tiles_n = (r.N + bn - 1) / bn;
@@ -562,7 +562,6 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     a.kb_per_split = kb_per; a.num_kb = num_kb;
     a.num_units = tiles_m * tiles_n * splits;
     a.half_from = a.num_units;  // no half tiles unless set below (one-CTA kernel)
-    a.grid_cap = sms;
     a.alpha = r.alpha;
     a.D = r.D; a.ldd = r.ldd;
     a.out_f16 = r.out_f16;
@@ -571,6 +570,25 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     const int vec_elems = r.out_f16 ? 8 : 4;
     a.vec_ok = ((reinterpret_cast<uintptr_t>(r.D) & 15u) == 0 && (r.ldd % vec_elems) == 0) ? 1 : 0;
     a.ws = splits > 1 ? static_cast<float*>(r.workspace) : nullptr;
+    if (r.n_peers > 0) {
+        // Tiles copied to other GPUs' D: the fused pair kernel's epilogue does it.
+        if (r.kind != GemmKind::kFused || r.n_peers > kMaxPeers || splits != 1) {
+            *why = "peer copies need an unsplit fused GEMM and at most 7 peers";
+            return cudaErrorInvalidValue;
+        }
+        a.n_peers = r.n_peers;
+        for (int i = 0; i < r.n_peers; ++i) a.peer_D[i] = r.peer_D[i];
+        const int clusters = fused_pair_capacity(r.a_fmt, dev);
+        switch (clusters > 0 ? r.a_fmt : -1) {
+            case kE4M3: return run_fused_pair<kE4M3>(r, a, clusters, st, why);
+            case kE5M2: return run_fused_pair<kE5M2>(r, a, clusters, st, why);
+            case kE2M1: return run_fused_pair<kE2M1>(r, a, clusters, st, why);
+            case kE2M1U: return run_fused_pair<kE2M1U>(r, a, clusters, st, why);
+            case kBF16: return run_fused_pair<kBF16>(r, a, clusters, st, why);
+            case kTF32: return run_fused_pair<kTF32>(r, a, clusters, st, why);
+            default: *why = "the fused pair kernel cannot run this format on this device"; return cudaErrorInvalidValue;
+        }
+    }
     if (r.kind == GemmKind::kNative) {
         const int ca = f8f6f4_code(r.a_fmt), cb = f8f6f4_code(r.b_fmt);
         if (ca < 0 || cb < 0) { *why = "native GEMM operands must be E4M3, E5M2 or E2M1_HW"; return cudaErrorInvalidValue; }
@@ -587,9 +605,9 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     const bool loading = r.kind == GemmKind::kF16 || r.kind == GemmKind::kNative || r.kind == GemmKind::kInt8;
     if (loading && bn == 256 && splits == 1 && r.M >= 256 && !r.force_bn && !r.force_splits) {
         const int mode = r.kind == GemmKind::kF16 ? kModeF16 : r.kind == GemmKind::kNative ? kModeNative8 : kModeInt8;
-        const int clusters = std::min(sms / 2, mode == kModeF16 ? pair_clusters<kModeF16>(dev)
-                                               : mode == kModeNative8 ? pair_clusters<kModeNative8>(dev)
-                                                                      : pair_clusters<kModeInt8>(dev));
+        const int clusters = mode == kModeF16 ? pair_clusters<kModeF16>(dev)
+                             : mode == kModeNative8 ? pair_clusters<kModeNative8>(dev)
+                                                    : pair_clusters<kModeInt8>(dev);
         if (clusters > 0) {
             // Bytes each CTA stages per k-block: 128 rows of A and 128 of B.
             auto row_bytes = [&](int f) -> uint32_t {
@@ -613,7 +631,7 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     // tiles enough not to split K, and fewer waves' worth of work than the
     // one-CTA kernel.
     if (r.kind == GemmKind::kFused && r.N >= 512 && splits == 1 && r.M >= 256 && !r.force_bn && !r.force_splits) {
-        const int clusters = std::min(sms / 2, fused_pair_capacity(r.a_fmt, dev));
+        const int clusters = fused_pair_capacity(r.a_fmt, dev);
         if (clusters > 0 && fused_pair_wins(r.a_fmt, r.M, r.N, clusters, sms)) {
             switch (r.a_fmt) {
                 case kE4M3: return run_fused_pair<kE4M3>(r, a, clusters, st, why);

@@ -52,6 +52,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include "tb_host.h"
 #include "tb_ptx.cuh"
 #include "tb_decode.cuh"
 
@@ -188,8 +189,11 @@ struct GemmArgs {
     // BN / 2-column halves of the tiles from half_from on (a partial last wave
     // split along N; == num_units when there are none).
     int half_from;
-    // Host side only: at most this many CTAs (SMs) for the launch (0: all).
-    int grid_cap;
+    // Fused pair kernel: after a tile's epilogue, copy its rows of D to the
+    // same place in each of these buffers (other GPUs' copies of D, mapped
+    // into this process).
+    int n_peers;
+    void* peer_D[kMaxPeers];
 };
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) ----------------------

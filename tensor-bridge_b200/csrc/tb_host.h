@@ -9,6 +9,9 @@
 
 namespace tb {
 
+// Other GPUs a fused pair GEMM can copy its output tiles to (one box of 8).
+constexpr int kMaxPeers = 7;
+
 // decode.cu
 cudaError_t decode_launch(int fmt, const void* src, uint16_t* dst, size_t n, cudaStream_t st, int sms);
 cudaError_t decode_transposed_launch(int fmt, const void* src, uint16_t* dst, int rows, int cols, cudaStream_t st);
@@ -42,7 +45,10 @@ struct GemmRequest {
     size_t workspace_bytes;
     int force_bn;       // 0 = choose automatically (for tests and tuning)
     int force_splits;   // 0 = choose automatically
-    int max_ctas;       // > 0: use at most this many SMs (leaves the rest to a concurrent kernel)
+    // Fused kind only: also copy every output tile to these other GPUs'
+    // buffers at D's offset (fused pair kernel; no split).
+    int n_peers;
+    void* const* peer_D;
 };
 
 // Split-K workspace needed by a fused/f16 GEMM of this shape (0 if none).
@@ -52,14 +58,15 @@ size_t gemm_workspace_bytes(GemmKind kind, int a_fmt, int M, int N, int K, int s
 // *why to a static message when the request itself is unsupported.
 cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why);
 
-// api.cu: tb_gemm_fused on at most max_ctas SMs (the sharded GEMM leaves the
-// other SMs to the concurrent NCCL all-gather).
-tb_status gemm_fused_capped(tb_format a_fmt, const void* A, const uint16_t* B, void* D, int M, int N, int K,
-                            tb_out_type out, float alpha, int max_ctas, tb_stream_t stream);
-
 // Block-scaled FP4 GEMM (kind::mxf4nvf4) on SM pairs; arguments validated by the caller.
 cudaError_t nvfp4_gemm_launch(const void* A, const uint8_t* sfa, const void* B, const uint8_t* sfb, void* D, int M,
                               int N, int K, int out_f16, float alpha, cudaStream_t st, const char** why);
+
+// api.cu: validated fused GEMM (D row stride N, no split) whose pair-kernel
+// epilogue also copies every output tile to the n_peers buffers peer_D, at
+// D's offset (other GPUs' copies of the output, mapped into this process).
+tb_status gemm_fused_to_peers(tb_format a_fmt, const void* A, const uint16_t* B, void* D, int M, int N, int K,
+                              tb_out_type out, float alpha, int n_peers, void* const* peer_D, tb_stream_t stream);
 
 // Device error word of the GEMM kernels (bounded-wait expiry).
 cudaError_t device_error_read(int* v);
