@@ -1,4 +1,4 @@
-"""Column-sharded fused GEMM over NCCL on two and four GPUs: every rank ends
+"""Column-sharded fused GEMM on two, four and eight GPUs: every rank ends
 with the whole D, bit-identical to the single-GPU fused GEMM (each row block is
 computed by the same kernel with the same K order) and within 1e-3 relative
 Frobenius error of the oracle.  Each world size needs that many GPUs and is
@@ -21,7 +21,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_sharded_fused(cuda, world):
     if cuda.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
