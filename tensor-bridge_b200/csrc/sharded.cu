@@ -357,10 +357,11 @@ tb_status tb_gemm_sharded_fused_p2p(tb_format a_fmt, const void* A_shard, const 
     tb_status st = barrier(pb, stream);
     for (int c = 0; c < chunks && st == TB_OK; ++c) {
         const size_t off = static_cast<size_t>(c * world + rank) * Mc * N * elem;  // this block's place in D
+        // Peers in the order rank + 1, rank + 2, ...: at any moment the ranks'
+        // epilogues store to different GPUs rather than all to the same one.
         void* peers[tb::kMaxPeers];
         int np = 0;
-        for (int r = 0; r < world; ++r)
-            if (r != rank) peers[np++] = pb.peer[r] + off;
+        for (int i = 1; i < world; ++i) peers[np++] = pb.peer[(rank + i) % world] + off;
         const void* ablk = static_cast<const char*>(A_shard) + c * a_block_bytes;
         st = tb::gemm_fused_to_peers(a_fmt, ablk, B, pb.local + off, Mc, N, K, out, alpha, np, peers, stream);
     }
