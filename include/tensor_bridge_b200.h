@@ -326,8 +326,12 @@ tb_status tb_gemm_sharded_fused_p2p(tb_format a_fmt, const void* A_shard, const 
 /* Collective over `comm`: maps every rank's `bytes`-byte device buffer `buf`
  * (a cudaMalloc allocation or part of one, 16-byte aligned, the same size on
  * all ranks) into every other rank's process with CUDA IPC, and returns the
- * handle for tb_gemm_sharded_fused_p2p.  Synchronises `stream`.  Fails on all
- * ranks (TB_ERR_INVALID_ARGUMENT or TB_ERR_CUDA) if it fails on one. */
+ * handle for tb_gemm_sharded_fused_p2p.  Synchronises `stream`.  A buffer
+ * that one rank cannot export, or that does not match on every rank, or a
+ * mapping that fails on one rank, fails the call on all ranks
+ * (TB_ERR_INVALID_ARGUMENT or TB_ERR_CUDA), after the same collectives; a
+ * failure before the exchange (an invalid argument, a 1 KB device allocation)
+ * returns on that rank alone, like any collective called on some ranks only. */
 tb_status tb_peer_buffer_register(void* comm, void* buf, size_t bytes, tb_stream_t stream, void** peer_buffer_out);
 /* Collective: waits (on `stream`, synchronised) until every rank has reached
  * it, then unmaps the peers' buffers.  Call it on every rank before any rank
