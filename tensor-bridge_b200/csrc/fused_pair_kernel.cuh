@@ -176,7 +176,9 @@ __device__ __forceinline__ void push_rows_to_peers(const GemmArgs& p, int row0, 
     }
 }
 
-template <class C>
+// PEERS: the instance that copies finished tiles to GemmArgs::peer_D (the
+// sharded GEMM); the plain instance carries none of that code.
+template <class C, bool PEERS = false>
 __global__ void __launch_bounds__(C::NUM_THREADS, 1)
     k_fused_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs p) {
     extern __shared__ uint8_t smem_raw[];
@@ -331,11 +333,12 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             }
             // Sharded output: copy the tile's rows to the other GPUs while the
             // MMAs of the next tile, which no longer need this accumulator, run.
-            if (p.n_peers > 0) push_rows_to_peers<C::BN>(p, tm * C::BM + my_row0 + quarter * 32, tn * C::BN, lane);
+            if constexpr (PEERS)
+                push_rows_to_peers<C::BN>(p, tm * C::BM + my_row0 + quarter * 32, tn * C::BN, lane);
         }
         // The peers read their D after the host's closing barrier: make this
         // warp's stores to them visible system-wide before the grid ends.
-        if (p.n_peers > 0) __threadfence_system();
+        if constexpr (PEERS) __threadfence_system();
     } else if (warp == 6) {
         // ---------------- TMA producer: this CTA's raw A rows ----------------
         int s = 0;

@@ -372,7 +372,18 @@ static cudaError_t run_fused_pair(const GemmRequest& r, const GemmArgs& args_in,
         return cudaErrorInvalidValue;
     }
     const int units = ((r.M + C::BM - 1) / C::BM) * ((r.N + C::BN - 1) / C::BN);
-    return launch_pairs<C>(k_fused_pair<C>, ta, tbm, args, units, clusters, st);
+    if (args.n_peers == 0) return launch_pairs<C>(k_fused_pair<C>, ta, tbm, args, units, clusters, st);
+    // The instance with the peer copies: same shared memory and threads, so
+    // the plain instance's cluster count holds for it.
+    static std::atomic<uint64_t> attr_done{0};
+    const uint64_t bit = 1ull << (current_device() & 63);
+    if (!(attr_done.load() & bit)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(k_fused_pair<C, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
+        if (e != cudaSuccess) return e;
+        attr_done.fetch_or(bit);
+    }
+    return launch_pairs<C>(k_fused_pair<C, true>, ta, tbm, args, units, clusters, st);
 }
 
 template <int BN, int MODE, int FMT>
