@@ -196,15 +196,18 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph ^ 1u, abort_flag))) { ok = false; break; }
                 if (elect_one()) {
-                    if (leader) mbar_arrive_expect_tx(&full[s], 2u * C::AB_BYTES);
-                    const uint32_t fb = leader_bar(&full[s]);
                     uint8_t* st = smem + s * C::STAGE_BYTES;
-                    tma_load_2d_pair(st, &tmA, fb, kb * 128, tm * C::BM + static_cast<int>(rank) * 128);
-                    tma_load_2d_pair(st + C::A_BYTES, &tmB, fb, kb * 128, tn * C::BN + static_cast<int>(rank) * 128);
-                    // Scale bytes: this CTA's A rows and all of the tile's B rows, on its own barrier.
+                    // Scale bytes first (this CTA's A rows and all of the tile's
+                    // B rows, on its own barrier): one SM's TMA requests land in
+                    // order, so the SF warps' copy to tensor memory then runs
+                    // while the stage's A and B are still arriving.
                     mbar_arrive_expect_tx(&sf_land[s], C::SF_BYTES);
                     tma_load_2d(st + C::AB_BYTES, &tmSA, &sf_land[s], kb * 16, tm * C::BM + static_cast<int>(rank) * 128);
                     tma_load_2d(st + C::AB_BYTES + C::SFA_BYTES, &tmSB, &sf_land[s], kb * 16, tn * C::BN);
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2u * C::AB_BYTES);
+                    const uint32_t fb = leader_bar(&full[s]);
+                    tma_load_2d_pair(st, &tmA, fb, kb * 128, tm * C::BM + static_cast<int>(rank) * 128);
+                    tma_load_2d_pair(st + C::A_BYTES, &tmB, fb, kb * 128, tn * C::BN + static_cast<int>(rank) * 128);
                 }
                 __syncwarp();
                 if (++s == C::S) { s = 0; ph ^= 1u; }
