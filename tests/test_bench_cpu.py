@@ -64,3 +64,22 @@ def test_targets_object_is_compact():
     assert t["skinny_pct_hbm_min_max"]["14336x4096_e4m3"] == [51.0, 66.0]
     assert t["sharded"]["check_pass"] is True
     assert len(json.dumps(t)) < 1200
+
+
+def test_targets_sharded_two_paths():
+    """On N GPUs the sharded section reports the peer-store path and, beside
+    it, the NCCL path; both reach the targets object with their checks."""
+    bench = _bench_module()
+    sq = {"pct_f16_dense_peak_nominal": 75.0}
+    formats = {k: {"fused_tflops": 1.0, "unfused_tflops": 2.0} for k in bench.FORMATS}
+    formats.update({f"native_{k}": {"pct_fp8_dense_peak": 50.0} for k in ("e4m3", "e2m1")})
+    check = {"pass": True, "rel_frob_max_vs_fp64": 2.08e-4}
+    line = {"fp4_8192_fused": sq, "fp4_8192_fused_after_load": sq, "e4m3_8192_fused": sq, "weight_only_mlp": [],
+            "formats": formats, "int8_4096": {"pct_i8_dense_peak": 40.0},
+            "sharded_weight_gemm": {"world": 8, "ms": 1.796, "gemm_only_ms": 1.166, "check": check,
+                                    "nccl": {"chunks": 4, "ms": 2.40, "allgather_only_ms": 1.34, "check": check}},
+            "config_256_e4m3": {"us": 12.3, "rel_frob_vs_unquantized_fp32": 0.0254}}
+    t = bench.targets(line)
+    assert t["sharded"]["world"] == 8 and t["sharded"]["ms"] == 1.796 and t["sharded"]["check_pass"] is True
+    assert t["sharded"]["nccl"] == {"ms": 2.4, "allgather_only_ms": 1.34, "check_pass": True}
+    assert len(json.dumps(t)) < 1200
