@@ -77,6 +77,8 @@ def test_shard_blocks_layout(tb):
     assert tb.shard_blocks(1024, 2, 2, 1) == [(256, 256), (768, 256)]
     # the 16384 x 53248 weight on 8 ranks: 4 chunks of 1664 rows (13 tiles)
     assert tb.shard_blocks(53248, 8, 4, 3)[1] == ((1 * 8 + 3) * 1664, 1664)
+    # one chunk (the peer-store path's layout): each rank's M / world contiguous rows
+    assert tb.shard_blocks(53248, 8, 1, 3) == [(3 * 6656, 6656)]
     with pytest.raises(ValueError):
         tb.shard_blocks(1000, 2, 2, 0)
     A = np.arange(1024 * 5, dtype=np.uint32).reshape(1024, 5)
