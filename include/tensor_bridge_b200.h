@@ -247,10 +247,15 @@ tb_status tb_gemm_nvfp4(const uint8_t* A, const uint8_t* A_scales, const uint8_t
 tb_status tb_fp4_repack_hw(const uint8_t* src, uint8_t* dst, size_t n_bytes, tb_stream_t stream);
 
 /* Mirror of gemm_fp8_fused_fp16 (src/gemm_fused.cu:24-49): A [M x K] E4M3,
- * B [K x N] E4M3 (row-major, as the reference reads it), D [M x N] FP32.
- * Both operands are decoded with the reference rules.  B is decoded and
- * transposed into `workspace` (N*K*2 bytes, see tb_gemm_fp8_fused_workspace),
- * A is decoded inside the GEMM. */
+ * B [K x N] E4M3 (row-major, as the reference reads it), D [M x N] FP32, the
+ * values of the reference's decode to FP16 and FP32-accumulated product.  Both
+ * operands being E4M3, it runs on the FP8 tensor cores (tb_gemm_native)
+ * without a decode: the codes of A, and of B transposed to [N x K], are
+ * copied into `workspace` (M*K + N*K bytes rounded up, see
+ * tb_gemm_fp8_fused_workspace) with the reference decoder's flush of the
+ * subnormal codes to zero applied, so the tensor core's exact products are
+ * those of the reference's FP16 operands.  A and the workspace 16-byte
+ * aligned. */
 tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, int M, int N, int K,
                                  void* workspace, size_t workspace_bytes, tb_stream_t stream);
 size_t tb_gemm_fp8_fused_workspace(int M, int N, int K);

@@ -309,10 +309,13 @@ tb_status tb_gemm_native(tb_format a_fmt, const void* A, tb_format b_fmt, const 
     return launch_gemm(r, stream);
 }
 
+// Workspace of tb_gemm_fp8_fused_fp16: the flushed copy of A [M x K] and the
+// flushed, transposed B [N x K], each 256-byte aligned.
+static size_t fp8_pair_bytes(int M, int K) { return (static_cast<size_t>(M) * K + 255) / 256 * 256; }
+
 size_t tb_gemm_fp8_fused_workspace(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    const size_t bt = (static_cast<size_t>(N) * K * 2 + 255) / 256 * 256;
-    return bt + tb_gemm_fused_workspace(TB_FMT_E4M3, M, N, K);
+    return fp8_pair_bytes(M, K) + fp8_pair_bytes(N, K);
 }
 
 // ---- INT8 path -------------------------------------------------------------------
@@ -388,14 +391,25 @@ tb_status tb_gemm_fp8_fused_fp16(const uint8_t* A, const uint8_t* B, float* D, i
     tb_status s = check_gemm_shape(M, N, K, TB_FMT_E4M3);
     if (s != TB_OK) return s;
     if (!A || !B || !D) return fail(TB_ERR_INVALID_ARGUMENT, "null pointer");
-    const size_t bt = (static_cast<size_t>(N) * K * 2 + 255) / 256 * 256;
-    if (!workspace || workspace_bytes < bt)
-        return fail(TB_ERR_WORKSPACE, "workspace needs at least %zu bytes", bt);
-    uint16_t* B16 = static_cast<uint16_t*>(workspace);
-    s = tb_decode_transposed(TB_FMT_E4M3, B, B16, K, N, stream);
+    const size_t need = tb_gemm_fp8_fused_workspace(M, N, K);
+    if (!workspace || workspace_bytes < need)
+        return fail(TB_ERR_WORKSPACE, "workspace needs at least %zu bytes", need);
+    if (!aligned16(A) || !aligned16(workspace)) return fail(TB_ERR_ALIGNMENT, "A and the workspace must be 16-byte aligned");
+    s = check_device();
     if (s != TB_OK) return s;
-    return tb_gemm_fused(TB_FMT_E4M3, A, B16, D, M, N, K, TB_OUT_F32, 1.0f, static_cast<uint8_t*>(workspace) + bt,
-                         workspace_bytes - bt, stream);
+    // Both operands are E4M3: the FP8 tensor cores multiply the codes
+    // directly.  The reference decodes them to FP16 first, flushing the
+    // subnormal codes to zero; the same flush applied to the codes (A copied,
+    // B copied into [N x K]) makes the tensor core's exact products those of
+    // the reference's FP16 operands.
+    uint8_t* Af = static_cast<uint8_t*>(workspace);
+    uint8_t* Bf = Af + fp8_pair_bytes(M, K);
+    const int sms = tb::device_info(tb::current_device()).sms;
+    s = from_cuda(tb::e4m3_flush_launch(A, Af, static_cast<size_t>(M) * K, stream, sms), "E4M3 flush launch");
+    if (s != TB_OK) return s;
+    s = from_cuda(tb::e4m3_flush_transposed_launch(B, Bf, K, N, stream), "E4M3 transposed flush launch");
+    if (s != TB_OK) return s;
+    return tb_gemm_native(TB_FMT_E4M3, Af, TB_FMT_E4M3, Bf, D, M, N, K, TB_OUT_F32, 1.0f, stream);
 }
 
 }  // extern "C"

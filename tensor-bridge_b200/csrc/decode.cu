@@ -249,13 +249,39 @@ __device__ __forceinline__ uint32_t e4m3x4_to_i8x4(uint32_t w, float scale) {
            (e4m3_to_i8_byte(static_cast<uint16_t>(h23 >> 16), scale) << 24);
 }
 
-// Streamer: 16 codes -> 16 INT8 per item, warp chunks of 32 x 4 consecutive
+// Four E4M3 codes with the reference decoder's subnormal rule applied in the
+// code domain: a code whose exponent field is zero becomes the signed zero
+// (sign bit kept), every other code (NaN included) stays.  The tensor core
+// then reads the codes with the values the reference's decode gives them.
+// Bit 7 of each byte of (w & 0x78787878) + 0x78787878 is set iff that code's
+// exponent is non-zero; times 0xFF per byte it becomes a byte mask.
+__device__ __forceinline__ uint32_t e4m3x4_flush_subnormals(uint32_t w) {
+    const uint32_t nz = ((w & 0x78787878u) + 0x78787878u) & 0x80808080u;
+    return w & (((nz >> 7) * 0xFFu) | 0x80808080u);
+}
+
+// Byte maps of the one-byte conversion kernels below: word() maps four codes,
+// byte() one code (in the low byte).
+struct ByteMapI8 {  // E4M3 -> INT8 of the reference's integer path
+    float scale;
+    __device__ __forceinline__ uint32_t word(uint32_t w) const { return e4m3x4_to_i8x4(w, scale); }
+    __device__ __forceinline__ uint32_t byte(uint8_t c) const {
+        return e4m3_to_i8_byte(tensor_bridge::e4m3_to_half_bits(c), scale);
+    }
+};
+struct ByteMapFlush {  // E4M3 -> E4M3 with the subnormal codes flushed
+    __device__ __forceinline__ uint32_t word(uint32_t w) const { return e4m3x4_flush_subnormals(w); }
+    __device__ __forceinline__ uint32_t byte(uint8_t c) const { return e4m3x4_flush_subnormals(c); }
+};
+
+// Streamer: 16 codes -> 16 bytes per item, warp chunks of 32 x 4 consecutive
 // items (contiguous 16-byte loads and stores); elements past the last whole
 // item one per thread.
-__global__ void __launch_bounds__(256) k_decode_e4m3_i8(const uint4* __restrict__ src, uint4* __restrict__ dst,
-                                                        size_t items, const uint8_t* __restrict__ tail_src,
-                                                        uint8_t* __restrict__ tail_dst, size_t tail_begin, size_t n,
-                                                        float scale) {
+template <class Map>
+__global__ void __launch_bounds__(256) k_e4m3_bytes(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                    size_t items, const uint8_t* __restrict__ tail_src,
+                                                    uint8_t* __restrict__ tail_dst, size_t tail_begin, size_t n,
+                                                    Map map) {
     constexpr int kRep = 4;
     constexpr size_t kChunk = 32 * kRep;
     const int lane = threadIdx.x & 31;
@@ -269,13 +295,11 @@ __global__ void __launch_bounds__(256) k_decode_e4m3_i8(const uint4* __restrict_
 #pragma unroll
         for (int j = 0; j < kRep; ++j)
             if (base + j * 32 + lane < items)
-                dst[base + j * 32 + lane] = make_uint4(e4m3x4_to_i8x4(in[j].x, scale), e4m3x4_to_i8x4(in[j].y, scale),
-                                                       e4m3x4_to_i8x4(in[j].z, scale), e4m3x4_to_i8x4(in[j].w, scale));
+                dst[base + j * 32 + lane] =
+                    make_uint4(map.word(in[j].x), map.word(in[j].y), map.word(in[j].z), map.word(in[j].w));
     }
     const size_t gt = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (tail_begin + gt < n)
-        tail_dst[tail_begin + gt] =
-            static_cast<uint8_t>(e4m3_to_i8_byte(tensor_bridge::e4m3_to_half_bits(tail_src[tail_begin + gt]), scale));
+    if (tail_begin + gt < n) tail_dst[tail_begin + gt] = static_cast<uint8_t>(map.byte(tail_src[tail_begin + gt]));
 }
 
 // src [rows x cols] -> dst [cols x rows] (the reference's B8[col * K + k]),
@@ -284,9 +308,9 @@ __global__ void __launch_bounds__(256) k_decode_e4m3_i8(const uint4* __restrict_
 // are 16-byte aligned), converts them, scatters the bytes into the transposed
 // tile, and then writes 16 bytes of one output row.  Edge tiles take bytes one
 // at a time.
-__global__ void __launch_bounds__(256) k_decode_e4m3_i8_transposed(const uint8_t* __restrict__ src,
-                                                                   uint8_t* __restrict__ dst, int rows, int cols,
-                                                                   float scale) {
+template <class Map>
+__global__ void __launch_bounds__(256) k_e4m3_bytes_transposed(const uint8_t* __restrict__ src,
+                                                               uint8_t* __restrict__ dst, int rows, int cols, Map map) {
     constexpr int PITCH = 80;  // 64 bytes + 16: keeps 16-byte alignment of tile rows
     __shared__ __align__(16) uint8_t tile[64 * PITCH];
     const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 64;
@@ -299,15 +323,14 @@ __global__ void __launch_bounds__(256) k_decode_e4m3_i8_transposed(const uint8_t
         const uint8_t* in = src + static_cast<size_t>(r) * cols + c;
         if (whole && (cols & 15) == 0 && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
             const uint4 q = *reinterpret_cast<const uint4*>(in);
-            w[0] = e4m3x4_to_i8x4(q.x, scale);
-            w[1] = e4m3x4_to_i8x4(q.y, scale);
-            w[2] = e4m3x4_to_i8x4(q.z, scale);
-            w[3] = e4m3x4_to_i8x4(q.w, scale);
+            w[0] = map.word(q.x);
+            w[1] = map.word(q.y);
+            w[2] = map.word(q.z);
+            w[3] = map.word(q.w);
         } else if (r < rows) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-                if (c + j < cols)
-                    w[j >> 2] |= e4m3_to_i8_byte(tensor_bridge::e4m3_to_half_bits(in[j]), scale) << (8 * (j & 3));
+                if (c + j < cols) w[j >> 2] |= (map.byte(in[j]) & 0xFFu) << (8 * (j & 3));
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) tile[(16 * v + j) * PITCH + lr] = static_cast<uint8_t>(w[j >> 2] >> (8 * (j & 3)));
@@ -532,8 +555,8 @@ cudaError_t decode_transposed_launch(int fmt, const void* src, uint16_t* dst, in
     }
 }
 
-cudaError_t decode_e4m3_i8_launch(const uint8_t* src, int8_t* dst, size_t n, float scale, cudaStream_t st, int sms) {
-    uint8_t* d = reinterpret_cast<uint8_t*>(dst);
+template <class Map>
+static cudaError_t launch_e4m3_bytes(const uint8_t* src, uint8_t* d, size_t n, Map map, cudaStream_t st, int sms) {
     const bool aligned = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(d)) & 15u) == 0;
     const size_t items = aligned ? n / 16 : 0;
     const size_t tail_begin = items * 16;
@@ -541,17 +564,35 @@ cudaError_t decode_e4m3_i8_launch(const uint8_t* src, int8_t* dst, size_t n, flo
     const size_t want = aligned ? (items + 1023) / 1024 : (n - tail_begin + 255) / 256;
     size_t blocks = std::min<size_t>(std::max<size_t>(want, 1), static_cast<size_t>(sms) * 8);
     if (!aligned) blocks = std::max<size_t>(want, 1);
-    k_decode_e4m3_i8<<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const uint4*>(src),
+    k_e4m3_bytes<Map><<<static_cast<unsigned>(blocks), 256, 0, st>>>(reinterpret_cast<const uint4*>(src),
                                                                      reinterpret_cast<uint4*>(d), items, src, d,
-                                                                     tail_begin, n, scale);
+                                                                     tail_begin, n, map);
     return cudaGetLastError();
+}
+
+template <class Map>
+static cudaError_t launch_e4m3_bytes_transposed(const uint8_t* src, uint8_t* dst, int rows, int cols, Map map,
+                                                cudaStream_t st) {
+    dim3 grid((cols + 63) / 64, (rows + 63) / 64);
+    k_e4m3_bytes_transposed<Map><<<grid, 256, 0, st>>>(src, dst, rows, cols, map);
+    return cudaGetLastError();
+}
+
+cudaError_t decode_e4m3_i8_launch(const uint8_t* src, int8_t* dst, size_t n, float scale, cudaStream_t st, int sms) {
+    return launch_e4m3_bytes(src, reinterpret_cast<uint8_t*>(dst), n, ByteMapI8{scale}, st, sms);
 }
 
 cudaError_t decode_e4m3_i8_transposed_launch(const uint8_t* src, int8_t* dst, int rows, int cols, float scale,
                                              cudaStream_t st) {
-    dim3 grid((cols + 63) / 64, (rows + 63) / 64);
-    k_decode_e4m3_i8_transposed<<<grid, 256, 0, st>>>(src, reinterpret_cast<uint8_t*>(dst), rows, cols, scale);
-    return cudaGetLastError();
+    return launch_e4m3_bytes_transposed(src, reinterpret_cast<uint8_t*>(dst), rows, cols, ByteMapI8{scale}, st);
+}
+
+cudaError_t e4m3_flush_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms) {
+    return launch_e4m3_bytes(src, dst, n, ByteMapFlush{}, st, sms);
+}
+
+cudaError_t e4m3_flush_transposed_launch(const uint8_t* src, uint8_t* dst, int rows, int cols, cudaStream_t st) {
+    return launch_e4m3_bytes_transposed(src, dst, rows, cols, ByteMapFlush{}, st);
 }
 
 cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms) {

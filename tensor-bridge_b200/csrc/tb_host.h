@@ -19,6 +19,11 @@ cudaError_t fp4_repack_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaSt
 cudaError_t decode_e4m3_i8_launch(const uint8_t* src, int8_t* dst, size_t n, float scale, cudaStream_t st, int sms);
 cudaError_t decode_e4m3_i8_transposed_launch(const uint8_t* src, int8_t* dst, int rows, int cols, float scale,
                                              cudaStream_t st);
+// E4M3 codes with the reference decoder's subnormal flush applied (a code
+// with exponent field 0 becomes the signed zero), as a copy and as a
+// transposed copy ([rows x cols] -> [cols x rows]).
+cudaError_t e4m3_flush_launch(const uint8_t* src, uint8_t* dst, size_t n, cudaStream_t st, int sms);
+cudaError_t e4m3_flush_transposed_launch(const uint8_t* src, uint8_t* dst, int rows, int cols, cudaStream_t st);
 cudaError_t decode_nvfp4_launch(const uint8_t* src, const uint8_t* scales, uint16_t* dst, size_t n,
                                 cudaStream_t st, int sms);
 size_t stored_bytes(int fmt, size_t n);

@@ -391,12 +391,23 @@ def test_native_fp4_matches_fused_after_repack(tb, cuda):
     check(native, fused, tol=1e-6)
 
 
-def test_fp8_fused_fp16_mirror(tb, cuda):
+@pytest.mark.parametrize("M,N,K,codes", [(512, 512, 512, "quantized"), (200, 72, 80, "all"),
+                                         (384, 136, 1040, "all")])
+def test_fp8_fused_fp16_mirror(tb, cuda, M, N, K, codes):
     """tb_gemm_fp8_fused_fp16 mirrors gemm_fp8_fused_fp16: both operands E4M3,
-    B given [K x N] row-major as the reference reads it."""
-    M, N, K = 512, 512, 512
-    a, b = O.uniform(20, (M, K)), O.uniform(21, (K, N))
-    A, Bkn = O.quantize(O.E4M3, a), O.quantize(O.E4M3, b)
+    B given [K x N] row-major as the reference reads it.  It runs on the FP8
+    tensor cores after flushing the subnormal codes the way the reference
+    decoder does; "all" draws both operands from every non-NaN code
+    (subnormals and the largest magnitudes included), on ragged shapes whose
+    B transpose has partial 64 x 64 tiles."""
+    if codes == "quantized":
+        a, b = O.uniform(20, (M, K)), O.uniform(21, (K, N))
+        A, Bkn = O.quantize(O.E4M3, a), O.quantize(O.E4M3, b)
+    else:
+        rng = np.random.default_rng(M + N + K)
+        pool = np.array([c for c in range(256) if c & 0x7F != 0x7F], dtype=np.uint8)
+        A = rng.choice(pool, size=(M, K)).astype(np.uint8)
+        Bkn = rng.choice(pool, size=(K, N)).astype(np.uint8)
     dA, dB = to_dev(cuda, A), to_dev(cuda, Bkn)
     ws_bytes = tb.lib().tb_gemm_fp8_fused_workspace(M, N, K)
     ws = empty_dev(cuda, ws_bytes)
