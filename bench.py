@@ -942,6 +942,23 @@ def profile_case(case: str):
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": case, "ok": True}))
         return
+    if fname.startswith("decode_"):  # a decode streamer on a ROWS x COLS weight (N(0, 0.02), per-tensor scale)
+        rows, cols = (int(v) for v in shape.lower().split("x"))
+        fmt = {"e4m3": tb.Format.E4M3, "e2m1": tb.Format.E2M1, "bf16": tb.Format.BF16,
+               "tf32": tb.Format.TF32}[fname[len("decode_"):]]
+        n = rows * cols
+        if fname[len("decode_"):] in FORMAT_MAX:
+            A, _ = weights_q(torch, tb, fmt, rows, cols, 0.02, seed=7)
+        else:
+            a = torch.randn(rows, cols, device="cuda") * 0.02
+            A = torch.empty(tb.stored_bytes(fmt, n), dtype=torch.uint8, device="cuda")
+            tb.quantize(fmt, a, A, n)
+        d = torch.empty(n, dtype=torch.float16, device="cuda")
+        for _ in range(5):
+            tb.decode(fmt, A, d, n)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": case, "ok": True}))
+        return
     M, N, K = (int(v) for v in shape.lower().split("x"))
     if fname == "nvfp4gemm":  # the block-scaled FP4 GEMM (kind::mxf4nvf4)
         g = torch.Generator(device="cuda")
@@ -1007,7 +1024,7 @@ def main():
                     help="run only 5 fused weight-only GEMMs of this case (e.g. e4m3:14336x16x4096; f16:MxNxK for "
                          "the plain FP16 GEMM, e4m3xe4m3:MxNxK for the native FP8 GEMM, nvfp4gemm:MxNxK for the "
                          "block-scaled FP4 GEMM, nvfp4:ROWSxCOLS for 5 "
-                         "block-scaled FP4 decodes) and exit; "
+                         "block-scaled FP4 decodes, decode_FMT:ROWSxCOLS for 5 decodes of one format) and exit; "
                          "the command profiles/ captures of single kernels use")
     args = ap.parse_args()
     if args.profile_case:
