@@ -71,7 +71,17 @@ def test_argument_validation_without_device(tb):
         tb.Status.UNSUPPORTED
     # fp8 mirror needs its workspace
     assert lib.tb_gemm_fp8_fused_fp16(p, p, p, 64, 64, 64, null, 0, null) == tb.Status.WORKSPACE
-    assert lib.tb_gemm_fp8_fused_workspace(64, 48, 64) >= 48 * 64 * 2
+    # flushed copies of A [M x K] and of B transposed [N x K], each rounded to 256 bytes
+    assert lib.tb_gemm_fp8_fused_workspace(64, 48, 64) == 64 * 64 + 48 * 64
+    assert lib.tb_gemm_fp8_fused_workspace(10, 3, 16) == 256 + 256
+    # peer buffers: nothing to release, and no GEMM or registration without a handle / communicator
+    # (TB_ERR_NCCL where NCCL cannot be loaded)
+    assert lib.tb_peer_buffer_release(null, null) == tb.Status.OK
+    st = lib.tb_gemm_sharded_fused_p2p(int(tb.Format.E4M3), p, p, null, 1024, 64, 64, 0, 1.0, 1, null)
+    assert st in (tb.Status.INVALID_ARGUMENT, tb.Status.NCCL)
+    h = ctypes.c_void_p()
+    st = lib.tb_peer_buffer_register(null, p, 1024, null, ctypes.byref(h))
+    assert st in (tb.Status.INVALID_ARGUMENT, tb.Status.NCCL) and not h.value
 
 
 def test_python_binding_raises(tb):
