@@ -161,18 +161,13 @@ __device__ __forceinline__ void settle_inflight_loads() {
 
 // Decode one 16-byte raw unit into WPU words of FP16 pairs (lower K first).
 // `scalar` (warp-uniform) selects the per-code path for units holding special
-// codes: E4M3 words with subnormal codes are flushed by mask and NaN words take
-// the reference rule; BF16 / TF32 specials take the reference rule.
+// codes: BF16 / TF32 specials take the reference rule.  E4M3 needs none
+// (decode_e4m3_x4_mma: every code's reference value, no branch).
 template <int FMT>
 __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, bool scalar) {
     if constexpr (FMT == kE4M3) {
-        if (scalar) {
-            decode_e4m3_x4(in.x, o[0], o[1]); decode_e4m3_x4(in.y, o[2], o[3]);
-            decode_e4m3_x4(in.z, o[4], o[5]); decode_e4m3_x4(in.w, o[6], o[7]);
-        } else {
-            decode_e4m3_x4_fast(in.x, o[0], o[1]); decode_e4m3_x4_fast(in.y, o[2], o[3]);
-            decode_e4m3_x4_fast(in.z, o[4], o[5]); decode_e4m3_x4_fast(in.w, o[6], o[7]);
-        }
+        decode_e4m3_x4_mma(in.x, o[0], o[1]); decode_e4m3_x4_mma(in.y, o[2], o[3]);
+        decode_e4m3_x4_mma(in.z, o[4], o[5]); decode_e4m3_x4_mma(in.w, o[6], o[7]);
     } else if constexpr (FMT == kE5M2) {
         decode_e5m2_x4(in.x, o[0], o[1]); decode_e5m2_x4(in.y, o[2], o[3]);
         decode_e5m2_x4(in.z, o[4], o[5]); decode_e5m2_x4(in.w, o[6], o[7]);
@@ -204,14 +199,11 @@ __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, 
     }
 }
 
-// Nonzero if a unit holds a code the fast path does not reproduce (E4M3,
-// BF16, TF32).
+// Nonzero if a unit holds a code the fast path does not reproduce (BF16,
+// TF32).
 template <int FMT>
 __device__ __forceinline__ uint32_t unit_special_mask(const uint4& in) {
-    if constexpr (FMT == kE4M3)
-        return (e4m3_special_bits(in.x) | e4m3_special_bits(in.y) | e4m3_special_bits(in.z) | e4m3_special_bits(in.w)) &
-               0x80808080u;
-    else if constexpr (FMT == kBF16)
+    if constexpr (FMT == kBF16)
         return bf16_nan_lanes(in.x) | bf16_nan_lanes(in.y) | bf16_nan_lanes(in.z) | bf16_nan_lanes(in.w);
     else if constexpr (FMT == kTF32)
         return max(tf32_max_mag(in.x, in.y), tf32_max_mag(in.z, in.w)) >= kTf32ScalarFrom ? 1u : 0u;
@@ -252,7 +244,7 @@ __device__ __forceinline__ void decode_kblock(uint32_t raw, int sub, int row, ui
 #pragma unroll
         for (int x = 0; x < C::UPH; ++x) in[x] = lds128(tmem_raw_addr<C>(raw, sub, row, h * C::UPH + x));
         bool scalar = false;
-        if constexpr (C::FMT == kE4M3 || C::FMT == kBF16 || C::FMT == kTF32) {
+        if constexpr (C::FMT == kBF16 || C::FMT == kTF32) {
             uint32_t m = 0;
 #pragma unroll
             for (int x = 0; x < C::UPH; ++x) m |= unit_special_mask<C::FMT>(in[x]);

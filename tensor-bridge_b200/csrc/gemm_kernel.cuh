@@ -216,15 +216,12 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
 }
 
 // True (warp-uniformly) if any lane's unit holds a code that the fast decode
-// path does not reproduce; those units take the per-code path (E4M3 subnormal
-// words flushed by mask, NaN words and BF16 NaNs by the reference rule).
+// path does not reproduce; those units take the per-code path (BF16 NaNs by
+// the reference rule).  E4M3 needs none: decode_e4m3_x4_mma gives every code
+// its reference value without a branch.
 template <int FMT>
 __device__ __forceinline__ bool unit_needs_scalar(const uint4& in) {
-    if constexpr (FMT == kE4M3) {
-        const uint32_t m = e4m3_special_mask(in.x) | e4m3_special_mask(in.y) | e4m3_special_mask(in.z) |
-                           e4m3_special_mask(in.w);
-        return __any_sync(0xFFFFFFFFu, m != 0u);
-    } else if constexpr (FMT == kBF16) {
+    if constexpr (FMT == kBF16) {
         const uint32_t m = bf16_nan_lanes(in.x) | bf16_nan_lanes(in.y) | bf16_nan_lanes(in.z) | bf16_nan_lanes(in.w);
         return __any_sync(0xFFFFFFFFu, m != 0u);
     } else {
@@ -239,13 +236,8 @@ __device__ __forceinline__ void decode_store_unit(const uint4& in, uint32_t dst,
     if constexpr (FMT == kE4M3 || FMT == kE5M2 || FMT == kE2M1U) {
         uint32_t o[8];  // 16 values -> FP16 chunks 2col, 2col+1
         if constexpr (FMT == kE4M3) {
-            if (unit_needs_scalar<kE4M3>(in)) {
-                decode_e4m3_x4(in.x, o[0], o[1]); decode_e4m3_x4(in.y, o[2], o[3]);
-                decode_e4m3_x4(in.z, o[4], o[5]); decode_e4m3_x4(in.w, o[6], o[7]);
-            } else {
-                decode_e4m3_x4_fast(in.x, o[0], o[1]); decode_e4m3_x4_fast(in.y, o[2], o[3]);
-                decode_e4m3_x4_fast(in.z, o[4], o[5]); decode_e4m3_x4_fast(in.w, o[6], o[7]);
-            }
+            decode_e4m3_x4_mma(in.x, o[0], o[1]); decode_e4m3_x4_mma(in.y, o[2], o[3]);
+            decode_e4m3_x4_mma(in.z, o[4], o[5]); decode_e4m3_x4_mma(in.w, o[6], o[7]);
         } else if constexpr (FMT == kE5M2) {
             decode_e5m2_x4(in.x, o[0], o[1]); decode_e5m2_x4(in.y, o[2], o[3]);
             decode_e5m2_x4(in.z, o[4], o[5]); decode_e5m2_x4(in.w, o[6], o[7]);

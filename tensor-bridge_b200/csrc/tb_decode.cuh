@@ -89,6 +89,19 @@ __device__ __forceinline__ void decode_e4m3_x4(uint32_t w, uint32_t& o0, uint32_
     else decode_e4m3_x4_scalar(w, o0, o1);
 }
 
+// For operands that only feed a tensor core: the reference decoder's value
+// for every code, with no branch.  The subnormal codes are flushed to their
+// signed zero in the code domain (bit 7 of each byte of (w & 0x78787878) +
+// 0x78787878 is set iff that code's exponent field is non-zero; prmt's
+// sign-replicating selectors turn it into a byte mask), then the hardware
+// converter runs.  A NaN code becomes an FP16 NaN of another payload than the
+// reference's 0x7E00 | sign, which changes nothing downstream: any product
+// with it is NaN.
+__device__ __forceinline__ void decode_e4m3_x4_mma(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    const uint32_t keep = prmt((w & 0x78787878u) + 0x78787878u, 0u, 0xBA98u);
+    decode_e4m3_x4_fast(w & (keep | 0x80808080u), o0, o1);
+}
+
 // ---- E5M2: each code is the top byte of its FP16 value -------------------------------
 
 __device__ __forceinline__ void decode_e5m2_x4(uint32_t w, uint32_t& o0, uint32_t& o1) {
