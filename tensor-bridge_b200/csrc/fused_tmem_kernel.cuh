@@ -160,9 +160,9 @@ __device__ __forceinline__ void settle_inflight_loads() {
 }
 
 // Decode one 16-byte raw unit into WPU words of FP16 pairs (lower K first).
-// `scalar` (warp-uniform) selects the per-code path for units holding special
-// codes: BF16 / TF32 specials take the reference rule.  E4M3 needs none
-// (decode_e4m3_x4_mma: every code's reference value, no branch).
+// `scalar` (warp-uniform) selects the per-code path for TF32 units holding
+// values at or above 2^16.  E4M3 and BF16 need none: their branch-free paths
+// give every code its reference value (a NaN only another FP16 payload).
 template <int FMT>
 __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, bool scalar) {
     if constexpr (FMT == kE4M3) {
@@ -181,13 +181,8 @@ __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, 
         decode_e2m1_packed_x8(in.z, t); o[8] = t[0]; o[9] = t[1]; o[10] = t[2]; o[11] = t[3];
         decode_e2m1_packed_x8(in.w, t); o[12] = t[0]; o[13] = t[1]; o[14] = t[2]; o[15] = t[3];
     } else if constexpr (FMT == kBF16) {
-        if (scalar) {
-            o[0] = decode_bf16_x2_scalar(in.x); o[1] = decode_bf16_x2_scalar(in.y);
-            o[2] = decode_bf16_x2_scalar(in.z); o[3] = decode_bf16_x2_scalar(in.w);
-        } else {
-            o[0] = decode_bf16_x2_fast(in.x); o[1] = decode_bf16_x2_fast(in.y);
-            o[2] = decode_bf16_x2_fast(in.z); o[3] = decode_bf16_x2_fast(in.w);
-        }
+        o[0] = decode_bf16_x2_fast(in.x); o[1] = decode_bf16_x2_fast(in.y);
+        o[2] = decode_bf16_x2_fast(in.z); o[3] = decode_bf16_x2_fast(in.w);
     } else if constexpr (FMT == kTF32) {
         if (scalar) {
             o[0] = decode_tf32_x2_scalar(in.x, in.y);
@@ -199,13 +194,10 @@ __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, 
     }
 }
 
-// Nonzero if a unit holds a code the fast path does not reproduce (BF16,
-// TF32).
+// Nonzero if a TF32 unit holds a value the fast path does not reproduce.
 template <int FMT>
 __device__ __forceinline__ uint32_t unit_special_mask(const uint4& in) {
-    if constexpr (FMT == kBF16)
-        return bf16_nan_lanes(in.x) | bf16_nan_lanes(in.y) | bf16_nan_lanes(in.z) | bf16_nan_lanes(in.w);
-    else if constexpr (FMT == kTF32)
+    if constexpr (FMT == kTF32)
         return max(tf32_max_mag(in.x, in.y), tf32_max_mag(in.z, in.w)) >= kTf32ScalarFrom ? 1u : 0u;
     else
         return 0u;
@@ -244,7 +236,7 @@ __device__ __forceinline__ void decode_kblock(uint32_t raw, int sub, int row, ui
 #pragma unroll
         for (int x = 0; x < C::UPH; ++x) in[x] = lds128(tmem_raw_addr<C>(raw, sub, row, h * C::UPH + x));
         bool scalar = false;
-        if constexpr (C::FMT == kBF16 || C::FMT == kTF32) {
+        if constexpr (C::FMT == kTF32) {
             uint32_t m = 0;
 #pragma unroll
             for (int x = 0; x < C::UPH; ++x) m |= unit_special_mask<C::FMT>(in[x]);

@@ -215,20 +215,12 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
     return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// True (warp-uniformly) if any lane's unit holds a code that the fast decode
-// path does not reproduce; those units take the per-code path (BF16 NaNs by
-// the reference rule).  E4M3 needs none: decode_e4m3_x4_mma gives every code
-// its reference value without a branch.
-template <int FMT>
-__device__ __forceinline__ bool unit_needs_scalar(const uint4& in) {
-    if constexpr (FMT == kBF16) {
-        const uint32_t m = bf16_nan_lanes(in.x) | bf16_nan_lanes(in.y) | bf16_nan_lanes(in.z) | bf16_nan_lanes(in.w);
-        return __any_sync(0xFFFFFFFFu, m != 0u);
-    } else {
-        return false;
-    }
-}
-
+// The decoded tiles only feed the tensor core, so E4M3 and BF16 take their
+// branch-free paths (decode_e4m3_x4_mma, decode_bf16_x2_fast): each gives
+// every code the reference decoder's value, and only a NaN's FP16 payload
+// differs from the reference's, which no product can show.  TF32 keeps its
+// per-pair test: its fast path would saturate values at or above 2^16 that
+// the reference turns into Inf.
 // Decode one 16-byte raw unit holding K slice `col` (in 16-byte raw units) of
 // tile row `row`, and store it into the swizzled FP16 tile at `dst`.
 template <int FMT>
@@ -259,13 +251,8 @@ __device__ __forceinline__ void decode_store_unit(const uint4& in, uint32_t dst,
         sts128(dst + swz(row, 4 * col + 3), o[0], o[1], o[2], o[3]);
     } else if constexpr (FMT == kBF16) {
         // 8 values -> FP16 chunk col
-        if (unit_needs_scalar<kBF16>(in)) {
-            sts128(dst + swz(row, col), decode_bf16_x2_scalar(in.x), decode_bf16_x2_scalar(in.y),
-                   decode_bf16_x2_scalar(in.z), decode_bf16_x2_scalar(in.w));
-        } else {
-            sts128(dst + swz(row, col), decode_bf16_x2_fast(in.x), decode_bf16_x2_fast(in.y),
-                   decode_bf16_x2_fast(in.z), decode_bf16_x2_fast(in.w));
-        }
+        sts128(dst + swz(row, col), decode_bf16_x2_fast(in.x), decode_bf16_x2_fast(in.y), decode_bf16_x2_fast(in.z),
+               decode_bf16_x2_fast(in.w));
     } else if constexpr (FMT == kTF32) {
         // 4 values -> half of FP16 chunk col/2
         sts64(dst + swz(row, col >> 1) + (col & 1) * 8, decode_tf32_x2(in.x, in.y), decode_tf32_x2(in.z, in.w));
