@@ -166,8 +166,8 @@ __device__ __forceinline__ void settle_inflight_loads() {
 template <int FMT>
 __device__ __forceinline__ void decode_unit_words(const uint4& in, uint32_t* o, bool scalar) {
     if constexpr (FMT == kE4M3) {
-        decode_e4m3_x4_mma(in.x, o[0], o[1]); decode_e4m3_x4_mma(in.y, o[2], o[3]);
-        decode_e4m3_x4_mma(in.z, o[4], o[5]); decode_e4m3_x4_mma(in.w, o[6], o[7]);
+        decode_e4m3_x4_scaled(in.x, o[0], o[1]); decode_e4m3_x4_scaled(in.y, o[2], o[3]);
+        decode_e4m3_x4_scaled(in.z, o[4], o[5]); decode_e4m3_x4_scaled(in.w, o[6], o[7]);
     } else if constexpr (FMT == kE5M2) {
         decode_e5m2_x4(in.x, o[0], o[1]); decode_e5m2_x4(in.y, o[2], o[3]);
         decode_e5m2_x4(in.z, o[4], o[5]); decode_e5m2_x4(in.w, o[6], o[7]);

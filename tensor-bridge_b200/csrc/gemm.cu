@@ -581,6 +581,7 @@ cudaError_t gemm_launch(const GemmRequest& r, cudaStream_t st, const char** why)
     const int vec_elems = r.out_f16 ? 8 : 4;
     a.vec_ok = ((reinterpret_cast<uintptr_t>(r.D) & 15u) == 0 && (r.ldd % vec_elems) == 0) ? 1 : 0;
     a.ws = splits > 1 ? static_cast<float*>(r.workspace) : nullptr;
+    if (r.kind == GemmKind::kFused && r.a_fmt == kE4M3) a.acc_shift = kE4M3AccShift;  // decode_e4m3_x4_scaled
     if (r.n_peers > 0) {
         // Tiles copied to other GPUs' D: the fused pair kernel's epilogue does it.
         if (r.kind != GemmKind::kFused || r.n_peers > kMaxPeers || splits != 1) {

@@ -194,6 +194,11 @@ struct GemmArgs {
     // into this process).
     int n_peers;
     void* peer_D[kMaxPeers];
+    // The accumulators hold D / alpha scaled by 2^-acc_shift (fused E4M3: the
+    // decoded weights carry 2^-8, decode_e4m3_x4_scaled); the epilogue
+    // multiplies them by 2^acc_shift, exactly, before alpha or the split-K
+    // partials.
+    int acc_shift;
 };
 
 // ---- explicit shared-memory accesses (32-bit shared addresses) ----------------------
@@ -216,9 +221,10 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
 }
 
 // The decoded tiles only feed the tensor core, so E4M3 and BF16 take their
-// branch-free paths (decode_e4m3_x4_mma, decode_bf16_x2_fast): each gives
-// every code the reference decoder's value, and only a NaN's FP16 payload
-// differs from the reference's, which no product can show.  TF32 keeps its
+// branch-free paths (decode_e4m3_x4_scaled, whose 2^-8 the epilogue undoes,
+// and decode_bf16_x2_fast): each gives every code the reference decoder's
+// value, and only a NaN's FP16 payload differs from the reference's, which
+// no product can show.  TF32 keeps its
 // per-pair test: its fast path would saturate values at or above 2^16 that
 // the reference turns into Inf.
 // Decode one 16-byte raw unit holding K slice `col` (in 16-byte raw units) of
@@ -228,8 +234,8 @@ __device__ __forceinline__ void decode_store_unit(const uint4& in, uint32_t dst,
     if constexpr (FMT == kE4M3 || FMT == kE5M2 || FMT == kE2M1U) {
         uint32_t o[8];  // 16 values -> FP16 chunks 2col, 2col+1
         if constexpr (FMT == kE4M3) {
-            decode_e4m3_x4_mma(in.x, o[0], o[1]); decode_e4m3_x4_mma(in.y, o[2], o[3]);
-            decode_e4m3_x4_mma(in.z, o[4], o[5]); decode_e4m3_x4_mma(in.w, o[6], o[7]);
+            decode_e4m3_x4_scaled(in.x, o[0], o[1]); decode_e4m3_x4_scaled(in.y, o[2], o[3]);
+            decode_e4m3_x4_scaled(in.z, o[4], o[5]); decode_e4m3_x4_scaled(in.w, o[6], o[7]);
         } else if constexpr (FMT == kE5M2) {
             decode_e5m2_x4(in.x, o[0], o[1]); decode_e5m2_x4(in.y, o[2], o[3]);
             decode_e5m2_x4(in.z, o[4], o[5]); decode_e5m2_x4(in.w, o[6], o[7]);
@@ -323,16 +329,18 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int sp, int r
         }
         return;
     }
+    const float sc = __int_as_float((127 + p.acc_shift) << 23);  // 2^acc_shift
+    auto val = [&](int j) { return __uint_as_float(v[j]) * sc; };
     if (p.splits > 1) {
         float* dst = p.ws + (static_cast<size_t>(sp) * p.M + row) * static_cast<size_t>(p.N) + col0;
         if (full && (p.N & 3) == 0) {
 #pragma unroll
             for (int j = 0; j < CW; j += 4)
-                *reinterpret_cast<uint4*>(dst + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                *reinterpret_cast<float4*>(dst + j) = make_float4(val(j), val(j + 1), val(j + 2), val(j + 3));
         } else {
 #pragma unroll
             for (int j = 0; j < CW; ++j)
-                if (col0 + j < p.N) dst[j] = __uint_as_float(v[j]);
+                if (col0 + j < p.N) dst[j] = val(j);
         }
         return;
     }
@@ -345,8 +353,7 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int sp, int r
                 uint32_t w[4];
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
-                    const __half2 t = __floats2half2_rn(__uint_as_float(v[j + 2 * h]) * a,
-                                                        __uint_as_float(v[j + 2 * h + 1]) * a);
+                    const __half2 t = __floats2half2_rn(val(j + 2 * h) * a, val(j + 2 * h + 1) * a);
                     w[h] = *reinterpret_cast<const uint32_t*>(&t);
                 }
                 *reinterpret_cast<uint4*>(dst + j) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -354,7 +361,7 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int sp, int r
         } else {
 #pragma unroll
             for (int j = 0; j < CW; ++j)
-                if (col0 + j < p.N) dst[j] = __float2half_rn(__uint_as_float(v[j]) * a);
+                if (col0 + j < p.N) dst[j] = __float2half_rn(val(j) * a);
         }
     } else {
         float* dst = static_cast<float*>(p.D) + static_cast<size_t>(row) * p.ldd + col0;
@@ -362,13 +369,12 @@ __device__ __forceinline__ void store_row_chunk(const GemmArgs& p, int sp, int r
 #pragma unroll
             for (int j = 0; j < CW; j += 4) {
                 *reinterpret_cast<float4*>(dst + j) =
-                    make_float4(__uint_as_float(v[j]) * a, __uint_as_float(v[j + 1]) * a,
-                                __uint_as_float(v[j + 2]) * a, __uint_as_float(v[j + 3]) * a);
+                    make_float4(val(j) * a, val(j + 1) * a, val(j + 2) * a, val(j + 3) * a);
             }
         } else {
 #pragma unroll
             for (int j = 0; j < CW; ++j)
-                if (col0 + j < p.N) dst[j] = __uint_as_float(v[j]) * a;
+                if (col0 + j < p.N) dst[j] = val(j) * a;
         }
     }
 }

@@ -89,18 +89,25 @@ __device__ __forceinline__ void decode_e4m3_x4(uint32_t w, uint32_t& o0, uint32_
     else decode_e4m3_x4_scalar(w, o0, o1);
 }
 
-// For operands that only feed a tensor core: the reference decoder's value
-// for every code, with no branch.  The subnormal codes are flushed to their
-// signed zero in the code domain (bit 7 of each byte of (w & 0x78787878) +
-// 0x78787878 is set iff that code's exponent field is non-zero; prmt's
-// sign-replicating selectors turn it into a byte mask), then the hardware
-// converter runs.  A NaN code becomes an FP16 NaN of another payload than the
+// For operands that only feed a tensor core whose accumulators are scaled
+// back by 2^8 (GemmArgs::acc_shift): the reference decoder's value of every
+// code times 2^-8, with no branch.  The hardware converter gives every code's
+// exact value (subnormal codes included); the multiplication by 2^-8 with
+// flush-to-zero is exact for the normal codes (at least 2^-6, which land at
+// 2^-14 or above) and sends the subnormal codes (below 2^-6) under FP16's
+// normal range, where .ftz makes them the signed zero the reference decoder
+// gives them.  A NaN code becomes an FP16 NaN of another payload than the
 // reference's 0x7E00 | sign, which changes nothing downstream: any product
-// with it is NaN.
-__device__ __forceinline__ void decode_e4m3_x4_mma(uint32_t w, uint32_t& o0, uint32_t& o1) {
-    const uint32_t keep = prmt((w & 0x78787878u) + 0x78787878u, 0u, 0xBA98u);
-    decode_e4m3_x4_fast(w & (keep | 0x80808080u), o0, o1);
+// with it is NaN.  Scaling every product by 2^-8 and the FP32 sum back by 2^8
+// is exact (no product of an FP16 value at least 2^-14 with an FP16 operand
+// comes near FP32's subnormal range), so D does not change.
+__device__ __forceinline__ void decode_e4m3_x4_scaled(uint32_t w, uint32_t& o0, uint32_t& o1) {
+    uint32_t h0, h1;
+    decode_e4m3_x4_fast(w, h0, h1);
+    asm("mul.rn.ftz.f16x2 %0, %1, %2;" : "=r"(o0) : "r"(h0), "r"(0x1C001C00u));  // 2^-8 in both halves
+    asm("mul.rn.ftz.f16x2 %0, %1, %2;" : "=r"(o1) : "r"(h1), "r"(0x1C001C00u));
 }
+constexpr int kE4M3AccShift = 8;
 
 // ---- E5M2: each code is the top byte of its FP16 value -------------------------------
 
@@ -154,8 +161,13 @@ __device__ __forceinline__ uint32_t swap_nibbles(uint32_t w) {
 
 // ---- BF16 ---------------------------------------------------------------------------
 
-// Lane mask from bit 15 of each 16-bit lane: 0xFFFF where set.
-__device__ __forceinline__ uint32_t lane_mask_bit15(uint32_t x) { return prmt(x, 0u, 0xBB99u); }
+// Two FP16 values times 1 with flush-to-zero: a subnormal becomes the zero of
+// its sign, every other value (zeros, normals, Inf) is unchanged.
+__device__ __forceinline__ uint32_t f16x2_flush_subnormal(uint32_t h) {
+    uint32_t r;
+    asm("mul.rn.ftz.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x3C003C00u));
+    return r;
+}
 
 // Two BF16 values (low lane first) -> two FP16 values.  Fast path: widen to
 // FP32 (exact), convert with the hardware FP32->FP16x2 converter (exact for
@@ -177,8 +189,7 @@ __device__ __forceinline__ uint32_t decode_bf16_x2_fast(uint32_t w) {
     const float hi = __uint_as_float(w & 0xFFFF0000u);
     uint32_t h;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
-    const uint32_t normal = lane_mask_bit15((h & 0x7C007C00u) + 0x7C007C00u);
-    return h & (normal | 0x80008000u);
+    return f16x2_flush_subnormal(h);
 }
 
 __device__ __forceinline__ uint32_t decode_bf16_x2(uint32_t w) {
@@ -218,8 +229,7 @@ constexpr uint32_t kTf32ScalarFrom = 143u << 23;
 __device__ __forceinline__ uint32_t decode_tf32_x2_fast(uint32_t t0, uint32_t t1) {
     uint32_t h;
     asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(__uint_as_float(t1)), "f"(__uint_as_float(t0)));
-    const uint32_t normal = lane_mask_bit15((h & 0x7C007C00u) + 0x7C007C00u);
-    return h & (normal | 0x80008000u);
+    return f16x2_flush_subnormal(h);
 }
 
 __device__ __forceinline__ uint32_t decode_tf32_x2(uint32_t t0, uint32_t t1) {
