@@ -568,6 +568,42 @@ def int8_square(torch, tb, n: int = 4096, iters: int = 10):
             "fp8_fused_int8_tops": ops / ms_f / 1e9}
 
 
+def rested(torch, section, pause_s: float = 2.0):
+    """Run `section()` after `pause_s` seconds of idle GPU; returns its result
+    and the SM clocks, power and throttle reasons sampled every 10 ms while it
+    ran."""
+    time.sleep(pause_s)
+    clocks = ClockSampler(torch.cuda.current_device(), interval_ms=10)
+    clocks.start()
+    res = section()
+    return res, clocks.stop()
+
+
+def native_square(torch, tb, n: int = 8192, iters: int = 20):
+    """Both operands quantized at n^3: E4M3 x E4M3 on tcgen05 kind::f8f6f4
+    (operands N(0, 1) with scale 448/maxabs each, alpha = 1/(sA sB)) and
+    INT8 x INT8 on kind::i8 (uniform over all codes, exact INT32 out); FP16
+    and INT32 outputs.  Dense FP8 / INT8 peak 4.5 P nominal."""
+    A, sa = weights_q(torch, tb, tb.Format.E4M3, n, n, 1.0, seed=81)
+    B, sb = weights_q(torch, tb, tb.Format.E4M3, n, n, 1.0, seed=82)
+    D = torch.empty(n, n, dtype=torch.float16, device="cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    al = float(np.float32(sa) * np.float32(sb))
+    ms = time_each(torch, lambda: tb.gemm_native(tb.Format.E4M3, A, tb.Format.E4M3, B, D, n, n, n, out=tb.Out.F16,
+                                                 alpha=al), iters, flush)
+    del A, B, D
+    g = torch.Generator(device="cuda")
+    g.manual_seed(83)
+    A8 = torch.randint(-128, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    B8 = torch.randint(-128, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    D32 = torch.empty(n, n, dtype=torch.int32, device="cuda")
+    ms_i8 = time_each(torch, lambda: tb.gemm_i8(A8, B8, D32, n, n, n), iters, flush)
+    ops = 2.0 * n ** 3
+    return {"M": n, "N": n, "K": n, "e4m3_ms": ms, "e4m3_tflops": ops / ms / 1e9,
+            "e4m3_pct_fp8_dense_peak": 100 * ops / ms / 1e9 / 4500.0, "i8_ms": ms_i8, "i8_tops": ops / ms_i8 / 1e9,
+            "i8_pct_i8_dense_peak": 100 * ops / ms_i8 / 1e9 / 4500.0}
+
+
 def fused_square(torch, tb, peaks, fmt_name: str = "e2m1", n: int = 8192, iters: int = 40):
     """Large square fused GEMM: A packed E2M1 (or E4M3) from N(0, 1) with scale
     FORMAT_MAX/maxabs, B FP16 N(0, 1), FP32 accumulation, FP16 output.  The SM
@@ -1118,11 +1154,17 @@ def main():
         torch.cuda.empty_cache()
         line["config_256_e4m3"] = config_256(torch, tb)
         torch.cuda.empty_cache()
-        line["nvfp4_8192"] = nvfp4_square(torch, tb)
-        torch.cuda.empty_cache()
+        # The next three sections start after a pause of two seconds, in the
+        # power state an idle GPU returns to, and record their own clocks:
+        # right after the large GEMMs above the GPU sits under its power cap
+        # at a lower SM clock.
+        for key, section in (("nvfp4_8192", nvfp4_square), ("native_8192", native_square)):
+            res, res["clocks"] = rested(torch, lambda: section(torch, tb))
+            line[key] = res
+            torch.cuda.empty_cache()
         line["decode_stream_14336x4096"] = decode_streams(torch, tb, peaks)
         torch.cuda.empty_cache()
-        line["weight_only_mlp"] = mlp_weight_only(torch, tb, peaks)
+        line["weight_only_mlp"], line["weight_only_mlp_clocks"] = rested(torch, lambda: mlp_weight_only(torch, tb, peaks))
         torch.cuda.empty_cache()
         line["int8_4096"] = int8_square(torch, tb)
         torch.cuda.empty_cache()
@@ -1164,6 +1206,9 @@ def targets(line: dict) -> dict:
     if nv:
         t["nvfp4_8192"] = {"tflops": r(nv["tflops"], 0), "pct_fp4_dense": r(nv["pct_fp4_dense_peak_nominal"])}
     t["int8_pct_i8_dense"] = r(line["int8_4096"]["pct_i8_dense_peak"])
+    nat = line.get("native_8192")
+    if nat:
+        t["native_8192_pct_dense"] = {"e4m3": r(nat["e4m3_pct_fp8_dense_peak"]), "i8": r(nat["i8_pct_i8_dense_peak"])}
     sh = line["sharded_weight_gemm"]
     t["sharded"] = {"world": sh["world"], "ms": r(sh["ms"], 3), "gemm_only_ms": r(sh.get("gemm_only_ms"), 3),
                     "check_pass": sh["check"]["pass"], "rel_frob": float(f"{sh['check']['rel_frob_max_vs_fp64']:.2e}")}

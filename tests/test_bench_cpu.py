@@ -59,9 +59,11 @@ def test_targets_object_is_compact():
             "formats": formats, "int8_4096": {"pct_i8_dense_peak": 40.0},
             "sharded_weight_gemm": {"world": 1, "ms": 9.9, "check": {"pass": True, "rel_frob_max_vs_fp64": 1e-6}},
             "config_256_e4m3": {"us": 5.0, "rel_frob_vs_unquantized_fp32": 0.025},
-            "cpu_baseline": {"naive_single_thread": {"256^3": {"ms": 15.0}, "512^3": {"ms": 120.0}}}}
+            "cpu_baseline": {"naive_single_thread": {"256^3": {"ms": 15.0}, "512^3": {"ms": 120.0}}},
+            "native_8192": {"e4m3_pct_fp8_dense_peak": 60.04, "i8_pct_i8_dense_peak": 55.55}}
     t = bench.targets(line)
     assert t["skinny_pct_hbm_min_max"]["14336x4096_e4m3"] == [51.0, 66.0]
+    assert t["native_8192_pct_dense"] == {"e4m3": 60.0, "i8": 55.5}
     assert t["sharded"]["check_pass"] is True
     assert len(json.dumps(t)) < 1200
 
