@@ -197,7 +197,8 @@ def launcher_rings(fmt, bn):
     nbr = nbr_g if 2 <= nbr_g < nbr_t else nbr_t
     sr = min(12, (avail - nbr * bround) // stage)
     sr = sr // spr * spr
-    inflight = sr - 1
+    cap = 65536 // stage if stage <= 16384 else sr - 1
+    inflight = min(sr - 1, cap)
     return rsk, sr, nrnd, inflight, nbr
 
 
