@@ -266,16 +266,44 @@ __global__ void __launch_bounds__(C::NUM_THREADS, 1)
             tc_fence_after();
             const int row = tm * C::BM + static_cast<int>(rank) * 128 + quarter * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+            if (p.out_f16 && p.vec_ok && tn * C::BN + C::BN <= p.N) {
+                // FP16 out, a whole aligned tile row: it fits in registers as
+                // FP16 pairs, so the accumulator is released before the global
+                // stores, which then overlap the next tile's MMAs.
+                uint32_t h[C::BN / 2];
+#pragma unroll
+                for (int c = 0; c < C::BN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(t_row + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const __half2 x = __floats2half2_rn(__uint_as_float(v[j]) * p.alpha,
+                                                            __uint_as_float(v[j + 1]) * p.alpha);
+                        h[(c + j) >> 1] = *reinterpret_cast<const uint32_t*>(&x);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(acc_empty, 0u);
+                if (row < p.M) {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.D) + static_cast<size_t>(row) * p.ldd +
+                                                          tn * C::BN);
+#pragma unroll
+                    for (int j = 0; j < C::BN / 8; ++j) dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+                }
+            } else {
 #pragma unroll 1
-            for (int c = 0; c < C::BN; c += 32) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(t_row + c, v);
-                tmem_wait_ld();
-                store_row_chunk<32>(p, 0, row, tn * C::BN + c, v);
+                for (int c = 0; c < C::BN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(t_row + c, v);
+                    tmem_wait_ld();
+                    store_row_chunk<32>(p, 0, row, tn * C::BN + c, v);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(acc_empty, 0u);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc_empty, 0u);
         }
     } else {
         // ---------------- SF warps: scale bytes, shared -> tensor memory ----------------
