@@ -472,7 +472,8 @@ def mlp_weight_only(torch, tb, peaks, iters: int = 20):
     launch streams its weight from HBM) inside a CUDA graph, median of 20
     replays; the few-token fused kernels of the sequence overlap their
     successor's start through programmatic dependent launch, as consecutive
-    layers would.  Algorithmic bytes = stored W + X + D."""
+    layers would.  Each weight's cases start after one second of idle GPU.
+    Algorithmic bytes = stored W + X + D."""
     out = []
     for (M, K) in ((14336, 4096), (4096, 14336)):
         for fname, fmt in (("e4m3", tb.Format.E4M3), ("e2m1", tb.Format.E2M1)):
@@ -481,6 +482,12 @@ def mlp_weight_only(torch, tb, peaks, iters: int = 20):
             As = [A] + [A.clone() for _ in range(copies - 1)]
             A16 = [torch.empty(M * K, dtype=torch.float16, device="cuda") for _ in range(2)]
             for N in (1, 16, 128, 2048):
+                if N == 1:
+                    # The previous weight's 2048-token GEMMs leave the GPU under
+                    # its power cap; a decode loop of few-token GEMMs runs
+                    # without them, so its cases start from an idle second.
+                    torch.cuda.synchronize()
+                    time.sleep(1.0)
                 g = torch.Generator(device="cuda")
                 g.manual_seed(N)
                 B = torch.randn(N, K, generator=g, device="cuda").half()
@@ -572,9 +579,10 @@ def rested(torch, section, pause_s: float = 2.0):
     """Run `section()` after `pause_s` seconds of idle GPU; returns its result
     and the SM clocks, power and throttle reasons sampled every 10 ms while it
     ran."""
-    time.sleep(pause_s)
     clocks = ClockSampler(torch.cuda.current_device(), interval_ms=10)
-    clocks.start()
+    clocks.start()  # nvidia-smi takes a moment to start sampling
+    time.sleep(pause_s)
+    clocks.lines.clear()  # keep only the samples taken while the section runs
     res = section()
     return res, clocks.stop()
 
