@@ -1167,7 +1167,8 @@ def main():
         # right after the large GEMMs above the GPU sits under its power cap
         # at a lower SM clock.
         for key, section in (("nvfp4_8192", nvfp4_square), ("native_8192", native_square)):
-            res, res["clocks"] = rested(torch, lambda: section(torch, tb))
+            res, clk = rested(torch, lambda: section(torch, tb))
+            res["clocks"] = clk
             line[key] = res
             torch.cuda.empty_cache()
         line["decode_stream_14336x4096"] = decode_streams(torch, tb, peaks)
