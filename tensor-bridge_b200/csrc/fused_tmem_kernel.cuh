@@ -96,8 +96,9 @@ struct TmemCfg {
     // ring at once gets all stages at about the same time, late, because HBM
     // serves the requests of all CTAs interleaved; a bounded number in flight
     // lands in order and the first round arrives early.  Measured best: 64 KB
-    // (four stages) for the 16 KB stages of packed FP4, whose ring holds ten;
-    // all but one stage of the ring (about 96 KB) for the 32 KB stages.
+    // (four stages) for the 16 KB stages of packed FP4, whose ring holds up to
+    // ten; all but one stage of the ring for the 32 KB stages (three of four
+    // for one-byte weights at 16 columns).
     // The stage waited for must not have been refilled yet: INFLIGHT < SR.
     static constexpr int INFLIGHT_CAP = STAGE_BYTES <= 16384 ? 65536 / STAGE_BYTES : SR - 1;
     static constexpr int INFLIGHT = SR - 1 < INFLIGHT_CAP ? SR - 1 : INFLIGHT_CAP;
@@ -145,6 +146,29 @@ struct TmemCfg {
     static_assert(NUM_THREADS <= 1024, "block size");
     static_assert(B_BYTES % 1024 == 0, "B tile alignment");
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+};
+
+// The launcher's choice of rings for a narrow tile of BN columns.  The B
+// ring gets about 64 KB (two to eight rounds), less if the raw ring would
+// otherwise hold fewer than NRND rounds (the decode groups' condition); the
+// raw ring the rest, up to twelve stages.
+template <int BN, int FMT>
+struct PickTmem {
+    static constexpr int NRND = BN <= 32 ? 3 : 2;  // round slots of TMEM A stages
+    static constexpr int ROW = raw_row_bytes(FMT);
+    static constexpr int RSK = ROW <= 64 ? 4 : ROW == 128 ? 2 : 1;
+    static constexpr int SPR = 4 / RSK;
+    static constexpr int STAGE = RSK * ROW * 128;
+    static constexpr int BROUND = 4 * BN * 128;
+    static constexpr int AVAIL = kSmemBudget - 1024;
+    static constexpr int NBR_T0 = 65536 / BROUND;
+    static constexpr int NBR_T = NBR_T0 > 8 ? 8 : (NBR_T0 < 2 ? 2 : NBR_T0);
+    static constexpr int NBR_G = (AVAIL - NRND * SPR * STAGE) / BROUND;  // most B rounds group mode allows
+    static constexpr int NBR = NBR_G >= 2 && NBR_G < NBR_T ? NBR_G : NBR_T;
+    static constexpr int SR0 = (AVAIL - NBR * BROUND) / STAGE;
+    static constexpr int SR1 = SR0 > 12 ? 12 : SR0;
+    static constexpr int SR = SR1 / SPR * SPR;
+    using Cfg = TmemCfg<BN, FMT, SR, NRND, NBR>;
 };
 
 // Shared-memory address of 16-byte raw unit `col` of k-block `sub` (position

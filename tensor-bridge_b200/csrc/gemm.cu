@@ -138,8 +138,6 @@ static bool make_raw_map(CUtensorMap* m, const void* A, uint64_t K, uint64_t M) 
 // ---------------------------------------------------------------------------------
 // Configurations
 
-constexpr int kSmemBudget = 224 * 1024;
-
 // Stage counts per configuration.  An operand-ring stage holds a B tile and
 // an A tile; fused mode adds a raw-A ring (whose stages also carry the B tiles
 // for narrow tiles, BN <= 64).  Fused: up to four operand stages and the rest
@@ -411,29 +409,6 @@ static cudaError_t run(const GemmRequest& r, const GemmArgs& args, cudaStream_t 
     }
     return launch_cfg<C>(ta, tbm, args, st, dev);
 }
-
-// Narrow fused tiles: decoded A goes to TMEM (fused_tmem_kernel.cuh).  The B
-// ring gets about 64 KB (two to eight rounds), less if the raw ring would
-// otherwise hold fewer than NRND rounds (the decode groups' condition); the
-// raw ring the rest, up to twelve stages.
-template <int BN, int FMT>
-struct PickTmem {
-    static constexpr int NRND = BN <= 32 ? 3 : 2;  // round slots of TMEM A stages
-    static constexpr int ROW = raw_row_bytes(FMT);
-    static constexpr int RSK = ROW <= 64 ? 4 : ROW == 128 ? 2 : 1;
-    static constexpr int SPR = 4 / RSK;
-    static constexpr int STAGE = RSK * ROW * 128;
-    static constexpr int BROUND = 4 * BN * 128;
-    static constexpr int AVAIL = kSmemBudget - 1024;
-    static constexpr int NBR_T0 = 65536 / BROUND;
-    static constexpr int NBR_T = NBR_T0 > 8 ? 8 : (NBR_T0 < 2 ? 2 : NBR_T0);
-    static constexpr int NBR_G = (AVAIL - NRND * SPR * STAGE) / BROUND;  // most B rounds group mode allows
-    static constexpr int NBR = NBR_G >= 2 && NBR_G < NBR_T ? NBR_G : NBR_T;
-    static constexpr int SR0 = (AVAIL - NBR * BROUND) / STAGE;
-    static constexpr int SR1 = SR0 > 12 ? 12 : SR0;
-    static constexpr int SR = SR1 / SPR * SPR;
-    using Cfg = TmemCfg<BN, FMT, SR, NRND, NBR>;
-};
 
 template <int BN, int FMT>
 static cudaError_t run_tmem(const GemmRequest& r, const GemmArgs& args, cudaStream_t st, int dev, const char** why) {

@@ -58,6 +58,10 @@
 
 namespace tb {
 
+// Dynamic shared memory the GEMM configurations plan their rings in (of the
+// 227 KB a CTA may use, leaving room for barriers and 1 KB alignment).
+constexpr int kSmemBudget = 224 * 1024;
+
 enum : int { kModeF16 = 0, kModeDecode = 1, kModeNative8 = 2, kModeInt8 = 3 };
 
 // Stored-format ids (same values as tb_format in the C header).

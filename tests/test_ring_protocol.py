@@ -18,7 +18,10 @@ model fails when that answer differs from the intended one (the phase
 completed or not), when an arrival lands in a phase other than the one it is
 meant for, or when no role can move.  The ring depths are the ones the
 launcher picks for each format and tile width, plus small rings."""
+import os
 import random
+import shutil
+import subprocess
 
 import pytest
 
@@ -203,6 +206,38 @@ def launcher_rings(fmt, bn):
 
 
 UNITS = [[64], [20, 28, 64, 12], [13, 9], [66, 10], [1, 2, 3, 5]]
+
+
+@pytest.fixture(scope="module")
+def library_rings(tmp_path_factory):
+    """The ring configurations the library itself picks, printed by
+    tests/tmem_cfg_probe.cu (host code built with nvcc; no GPU needed)."""
+    if shutil.which("nvcc") is None:
+        pytest.skip("nvcc not available")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path_factory.mktemp("probe") / "tmem_cfg_probe")
+    subprocess.run(["nvcc", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+                    "-I" + os.path.join(root, "include"), "-I" + os.path.join(root, "tensor-bridge_b200", "csrc"),
+                    os.path.join(root, "tests", "tmem_cfg_probe.cu"), "-o", exe],
+                   check=True, capture_output=True, timeout=600)
+    out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=60).stdout
+    rows = {}
+    for line in out.split("\n"):
+        if line.strip():
+            f = line.split()
+            rows[(f[0], int(f[1]))] = tuple(int(v) for v in f[2:])
+    return rows
+
+
+def test_model_rings_are_the_librarys(library_rings):
+    """The Python copy of the launcher's ring rules (launcher_rings) gives the
+    library's own choices, so the protocol model runs the rings the kernel
+    runs."""
+    assert library_rings
+    for (fmt, bn), (rsk, sr, nrnd, nbr, inflight, groups) in library_rings.items():
+        m_rsk, m_sr, m_nrnd, m_inflight, m_nbr = launcher_rings(fmt, bn)
+        assert (m_rsk, m_sr, m_nrnd, m_nbr, m_inflight) == (rsk, sr, nrnd, nbr, inflight), (fmt, bn)
+        assert groups == (1 if m_sr // (DK // m_rsk) >= m_nrnd else 0), (fmt, bn)
 
 
 @pytest.mark.parametrize("fmt", list(ROW_BYTES))
