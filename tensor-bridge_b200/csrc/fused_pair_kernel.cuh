@@ -96,6 +96,19 @@ struct FusedPairCfg {
     static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
+// The launcher's rings for the fused 256 x 512 SM-pair tiles:
+// four operand stages of 48 KB (this CTA's decoded A tile and 256 B rows; TF32
+// three, for two 32 KB raw stages) and the rest of shared memory for the raw
+// ring.
+template <int FMT>
+struct PickFusedPair {
+    static constexpr int S = FMT == kTF32 ? 3 : 4;
+    static constexpr int SA0 = (kSmemBudget - S * 3 * 128 * 128) / raw_stage_bytes(FMT);
+    static constexpr int SA = SA0 > 8 ? 8 : SA0;
+    static constexpr int DK = raw_kblocks(FMT) < 2 ? raw_kblocks(FMT) : 2;
+    using Cfg = FusedPairCfg<FMT, S, SA, DK>;
+};
+
 // Pair tile u -> (tile row, tile column).  The operand that every wave of
 // clusters reads whole stays in L2 across waves: with M tiles varying fastest
 // a wave covers all rows of A and a few B columns, so A should be the smaller

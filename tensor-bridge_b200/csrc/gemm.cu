@@ -294,19 +294,6 @@ static cudaError_t run_pair(const GemmRequest& r, const GemmArgs& args, int clus
     return launch_pairs<C>(k_gemm_pair<C>, ta, tbm, a, units, clusters, st);
 }
 
-// Fused decode + GEMM on 256 x 512 SM-pair tiles (fused_pair_kernel.cuh):
-// four operand stages of 48 KB (this CTA's decoded A tile and 256 B rows; TF32
-// three, for two 32 KB raw stages) and the rest of shared memory for the raw
-// ring.
-template <int FMT>
-struct PickFusedPair {
-    static constexpr int S = FMT == kTF32 ? 3 : 4;
-    static constexpr int SA0 = (kSmemBudget - S * 3 * 128 * 128) / raw_stage_bytes(FMT);
-    static constexpr int SA = SA0 > 8 ? 8 : SA0;
-    static constexpr int DK = raw_kblocks(FMT) < 2 ? raw_kblocks(FMT) : 2;
-    using Cfg = FusedPairCfg<FMT, S, SA, DK>;
-};
-
 template <int FMT>
 static int fused_pair_clusters(int dev) {
     using C = typename PickFusedPair<FMT>::Cfg;

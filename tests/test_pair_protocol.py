@@ -25,7 +25,7 @@ import random
 
 import pytest
 
-from test_ring_protocol import Bar
+from test_ring_protocol import Bar, library_ring_lines
 
 ND = 2  # decode warps per CTA in the model (the kernel has 8 or 16)
 NE = 2  # epilogue warps per CTA in the model (the kernel has 4)
@@ -166,6 +166,18 @@ def test_launcher_rings(fmt, num_kb, units):
     assert sa >= 2
     for seed in range(3):
         run(num_kb, units, rk, s, sa, dk, seed=seed)
+
+
+def test_model_rings_are_the_librarys():
+    """The Python copy of the launcher's ring rules (launcher_rings) gives the
+    library's own choices (tests/ring_cfg_probe.cu)."""
+    lines = library_ring_lines()
+    if lines is None:
+        pytest.skip("nvcc not available")
+    pairs = {f[1]: tuple(int(v) for v in f[2:]) for f in lines if f[0] == "PAIR"}
+    assert set(pairs) == set(RAW)
+    for fmt, cfg in pairs.items():
+        assert launcher_rings(fmt) == cfg, fmt
 
 
 @pytest.mark.parametrize("rk,s,sa,dk", [(4, 2, 2, 1), (4, 3, 2, 2), (2, 3, 3, 2), (1, 2, 2, 1), (4, 5, 2, 4)])

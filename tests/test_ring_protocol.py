@@ -18,10 +18,12 @@ model fails when that answer differs from the intended one (the phase
 completed or not), when an arrival lands in a phase other than the one it is
 meant for, or when no role can move.  The ring depths are the ones the
 launcher picks for each format and tile width, plus small rings."""
+import functools
 import os
 import random
 import shutil
 import subprocess
+import tempfile
 
 import pytest
 
@@ -208,25 +210,30 @@ def launcher_rings(fmt, bn):
 UNITS = [[64], [20, 28, 64, 12], [13, 9], [66, 10], [1, 2, 3, 5]]
 
 
-@pytest.fixture(scope="module")
-def library_rings(tmp_path_factory):
-    """The ring configurations the library itself picks, printed by
-    tests/tmem_cfg_probe.cu (host code built with nvcc; no GPU needed)."""
+@functools.lru_cache(maxsize=1)
+def library_ring_lines():
+    """The ring configurations the library itself picks, as printed by
+    tests/ring_cfg_probe.cu (host code built with nvcc; no GPU needed):
+    {(kind, format, ...): values}.  None without nvcc."""
     if shutil.which("nvcc") is None:
-        pytest.skip("nvcc not available")
+        return None
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    exe = str(tmp_path_factory.mktemp("probe") / "tmem_cfg_probe")
-    subprocess.run(["nvcc", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
-                    "-I" + os.path.join(root, "include"), "-I" + os.path.join(root, "tensor-bridge_b200", "csrc"),
-                    os.path.join(root, "tests", "tmem_cfg_probe.cu"), "-o", exe],
-                   check=True, capture_output=True, timeout=600)
-    out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=60).stdout
-    rows = {}
-    for line in out.split("\n"):
-        if line.strip():
-            f = line.split()
-            rows[(f[0], int(f[1]))] = tuple(int(v) for v in f[2:])
-    return rows
+    with tempfile.TemporaryDirectory() as tmp:
+        exe = os.path.join(tmp, "ring_cfg_probe")
+        subprocess.run(["nvcc", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+                        "-I" + os.path.join(root, "include"), "-I" + os.path.join(root, "tensor-bridge_b200", "csrc"),
+                        os.path.join(root, "tests", "ring_cfg_probe.cu"), "-o", exe],
+                       check=True, capture_output=True, timeout=600)
+        out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=60).stdout
+    return [line.split() for line in out.splitlines() if line.strip()]
+
+
+@pytest.fixture(scope="module")
+def library_rings():
+    lines = library_ring_lines()
+    if lines is None:
+        pytest.skip("nvcc not available")
+    return {(f[1], int(f[2])): tuple(int(v) for v in f[3:]) for f in lines if f[0] == "TMEM"}
 
 
 def test_model_rings_are_the_librarys(library_rings):
